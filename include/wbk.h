@@ -1,0 +1,151 @@
+/*
+ * wbk.h — C ABI of libwbk.so, the B200 (sm_100a) kernels behind the
+ * `whisper_blaze_kernels` op surface of whisper-blaze.
+ *
+ * Conventions
+ *   - Every entry point is asynchronous on `stream` (a cudaStream_t / CUstream;
+ *     NULL = legacy default stream) and runs on the CURRENT CUDA device. All
+ *     pointers are device pointers unless a parameter says "host".
+ *   - Return value: WBK_OK (0) or a WBK_ERR_* code; wbk_last_error() returns a
+ *     thread-local human-readable message for the most recent failure.
+ *   - Argument errors are detected on the host before anything is launched,
+ *     so a failing call never leaves partial work on the stream.
+ *   - fp16 = IEEE binary16, fp8 = OCP E4M3FN / E5M2 bytes (uint8 storage).
+ *   - No entry point allocates memory or synchronises the device, except
+ *     wbk_device_error() which reads a flag back (it synchronises).
+ *
+ * Citations are to the reference project techbysaurabh/whisper-blaze v0.1.17.
+ */
+#ifndef WBK_H_
+#define WBK_H_
+
+#include <stdint.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* wbk_stream_t;
+
+/* status codes */
+#define WBK_OK                   0
+#define WBK_ERR_INVALID_ARG      1   /* bad pointer / size / alignment / enum */
+#define WBK_ERR_UNSUPPORTED      2   /* shape or device outside what the kernel supports */
+#define WBK_ERR_CUDA             3   /* a CUDA runtime/driver call failed */
+#define WBK_ERR_DEVICE_TIMEOUT   4   /* a bounded device-side wait gave up (see wbk_device_error) */
+
+/* fp8 formats */
+#define WBK_FMT_E4M3 0
+#define WBK_FMT_E5M2 1
+
+/* GEMM epilogues */
+#define WBK_EPI_NONE          0   /* out = fp16(acc*descale [+ bias]) */
+#define WBK_EPI_GELU          1   /* out = fp16(gelu_erf(acc*descale + bias)) */
+#define WBK_EPI_RESIDUAL      2   /* out = fp16(acc*descale + bias + residual) */
+#define WBK_EPI_RESIDUAL_CLAMP 3  /* as RESIDUAL, then clamp to +-(65504-1000) (HF fp16 encoder clamp) */
+
+/* ---------------------------------------------------------------- misc */
+
+/* Library ABI version (major*10000 + minor*100 + patch). */
+int wbk_version(void);
+
+/* Thread-local message describing the last failing call on this thread. */
+const char* wbk_last_error(void);
+
+/* Read (and clear) the device-side error word of the current device that the
+ * bounded waits inside the GEMM kernel set when they give up. Synchronises the
+ * current device. *code_out = 0 when no device-side error happened. */
+int wbk_device_error(uint32_t* code_out);
+
+/* Self-test of the bounded-wait machinery: launches one CTA that waits on an
+ * mbarrier nothing ever arrives on, for at most `timeout_ns`, and records
+ * WBK_ERR_DEVICE_TIMEOUT in the device error word. Used by tests to prove that
+ * a wait which runs out returns a status instead of hanging. */
+int wbk_selftest_bounded_wait(uint64_t timeout_ns, wbk_stream_t stream);
+
+/* ------------------------------------------------------------ quantiser */
+
+/* Max-accumulate max(|x|) over n fp16 values into *amax_bits, which holds the
+ * fp16 bit pattern of the running maximum in its low 16 bits (uint32 so it can
+ * be updated with atomicMax). NaNs are ignored (as fmaxf does in the
+ * reference). The caller zeroes *amax_bits before the first accumulation.
+ * Replaces: compute_scale_kernel, csrc/kernels/fp8_quantize.cu:45-74, and the
+ * host block-max loop of compute_fp8_scale, fp8_quantize.cu:194-219. */
+int wbk_amax_f16(const void* x, int64_t n, uint32_t* amax_bits, wbk_stream_t stream);
+
+/* Given an accumulated *amax_bits, compute the per-tensor scale exactly as the
+ * reference does — scale = amax / max_fp8 (fast-math division, as compiled by
+ * the reference), 1.0 when that is not > 0 — and inv_scale = 1/scale rounded
+ * to nearest; write scale to scale_out[0] (device float, may be NULL) and
+ * quantise: q = fp8_rn_satfinite(clamp(float(x)*inv_scale, -max_fp8, max_fp8)).
+ * fmt = WBK_FMT_E4M3 (max 448) or WBK_FMT_E5M2 (max 57344). Any n >= 0.
+ * Replaces: quantise_fp16_to_e4m3_kernel / _e5m2_kernel, fp8_quantize.cu:81-137,
+ * and quantise_to_e4m3 / quantise_to_e5m2, fp8_quantize.cu:222-257. */
+int wbk_quantise_from_amax_f16(const void* x, int64_t n, int fmt,
+                               const uint32_t* amax_bits, void* q_out,
+                               float* scale_out, wbk_stream_t stream);
+
+/* Convenience: zero *amax_ws, accumulate amax, then quantise (three stream
+ * operations, no host synchronisation). amax_ws is a caller-owned device
+ * uint32 used as the accumulator.
+ * Replaces: quantise_to_e4m3 / quantise_to_e5m2, fp8_quantize.cu:222-257
+ * (without its device->host copy of per-block partials, fp8_quantize.cu:212). */
+int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out,
+                     float* scale_out, uint32_t* amax_ws, wbk_stream_t stream);
+
+/* out = fp16(float(q) * scale) for n fp8 values; scale is a host float.
+ * Replaces: dequantise_e4m3_to_fp16_kernel / _e5m2, fp8_quantize.cu:143-187,
+ * and dequantise_e4m3 / dequantise_e5m2, fp8_quantize.cu:260-291. */
+int wbk_dequantise_f16(const void* q, int64_t n, int fmt, float scale,
+                       void* out, wbk_stream_t stream);
+
+/* ------------------------------------------------------------- norms */
+
+/* Row-wise over [rows, D] fp16, D % 8 == 0:
+ *   s = x (+ residual);  out = fp16((s - mean) * rsqrt(var + eps) * gamma + beta)
+ *   sum_out (may be NULL) = fp16(s)
+ *   out_amax_bits (may be NULL): max-accumulate max|out| (fp16 bits), for a
+ *   following wbk_quantise_from_amax_f16 without another pass over `out`.
+ * residual may be NULL (plain LayerNorm).
+ * Replaces: layernorm_fused_kernel + layernorm_fused_impl,
+ * csrc/kernels/layernorm_fused.cu:50-184, :266-300 (bound as layernorm_fused /
+ * layernorm_fused_residual, csrc/ops/bindings.cpp:101-135). */
+int wbk_layernorm_f16(const void* x, const void* residual, const void* gamma,
+                      const void* beta, void* out, void* sum_out,
+                      int64_t rows, int64_t D, float eps,
+                      uint32_t* out_amax_bits, wbk_stream_t stream);
+
+/* out = fp16((x + residual) * rsqrt(mean((x+residual)^2) + eps) * gamma),
+ * residual required, D % 8 == 0.
+ * Replaces: rmsnorm_fused_kernel + rmsnorm_fused,
+ * csrc/kernels/layernorm_fused.cu:191-258, :312-335. */
+int wbk_rmsnorm_f16(const void* x, const void* residual, const void* gamma,
+                    void* out, int64_t rows, int64_t D, float eps,
+                    wbk_stream_t stream);
+
+/* --------------------------------------------------------------- GEMM */
+
+/* FP8 x FP8 -> fp32 (TMEM) -> fp16 scaled GEMM on tcgen05 tensor cores:
+ *   out[M,N] = epilogue( (sum_k A[m,k] * W[n,k]) * descale (+ bias[n]) ... )
+ *   descale = alpha * (a_scale ? *a_scale : 1) * (w_scale ? *w_scale : 1)
+ * A [M,K] and W [N,K] are row-major fp8 (K contiguous, the nn.Linear weight
+ * layout), formats a_fmt / w_fmt (WBK_FMT_*); K % 16 == 0 and both base
+ * pointers 16-byte aligned (TMA). bias fp16 [N] or NULL; residual fp16 [M,N]
+ * (row stride N) required for the RESIDUAL epilogues; out fp16 [M,N].
+ * out_amax_bits (may be NULL): max-accumulate max|out| as fp16 bits.
+ * Replaces the intent of gemm_fp8_e4m3_kernel / gemm_fp8_e4m3,
+ * csrc/kernels/gemm_hopper.cu:179-269, :298-322 (never bound in the
+ * reference), and the dequantise + F.linear of BlazeLinear.forward,
+ * whisper_blaze/model.py:80-109. */
+int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K,
+                 int a_fmt, int w_fmt, float alpha,
+                 const float* a_scale, const float* w_scale,
+                 const void* bias, const void* residual, void* out,
+                 int epilogue, uint32_t* out_amax_bits, wbk_stream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* WBK_H_ */

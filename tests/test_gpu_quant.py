@@ -1,0 +1,175 @@
+"""GPU parity of the quantiser / dequantiser (calls go through the C ABI).
+
+Gate: FP8 bytes and scales bit-exact.
+  * bytes: against the oracle's element rule (oracle/fp8.py), given the scale;
+  * scale: against the reference CUDA quantiser's own scale — live from
+    oracle/_ref when that build is present, and always against the golden table
+    of the reference scale for every positive finite fp16 amax
+    (tests/golden/ref_scale_table.npz) — and within 1 ulp of the IEEE quotient.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN_DIR, randn_f16
+from oracle import fp8
+from whisper_blaze_b200 import _lib, ops
+
+pytestmark = pytest.mark.gpu
+
+
+def _special_values(n=4096, seed=7):
+    g = torch.Generator().manual_seed(seed)
+    bits = torch.randint(0, 65536, (n,), generator=g, dtype=torch.int32).to(torch.int16)
+    x = bits.view(torch.float16).clone()
+    x[:8] = torch.tensor([0.0, -0.0, float("nan"), float("inf"), -float("inf"), 65504.0, -65504.0, 6e-8])
+    return x
+
+
+def _cases():
+    yield "randn_1500x1280", randn_f16((1500, 1280), 100)
+    yield "weights_5120x1280", randn_f16((5120, 1280), 101, std=0.02)
+    yield "randn_64x1280", randn_f16((64, 1280), 102)
+    yield "ragged_7", randn_f16((7,), 103)
+    yield "ragged_13", randn_f16((13,), 104)
+    yield "ragged_4099", randn_f16((4099,), 105)
+    yield "single", torch.tensor([0.75], dtype=torch.float16)
+    yield "zeros", torch.zeros(4096, dtype=torch.float16)
+    yield "specials", _special_values()
+    yield "finite_no_inf", torch.nan_to_num(_special_values(seed=8), posinf=0.0, neginf=0.0)
+    yield "tiny", (randn_f16((1024,), 106) * 1e-6).half()
+    yield "huge", (randn_f16((1024,), 107) * 20000).half()
+
+
+CASES = list(_cases())
+
+
+@pytest.mark.parametrize("fmt_name", ["e4m3", "e5m2"])
+@pytest.mark.parametrize("name,x", CASES, ids=[c[0] for c in CASES])
+def test_quantise_bit_exact(cuda_device, name, x, fmt_name):
+    fmt = fp8.FMT_NAMES[fmt_name]
+    q, s = ops.quantise(x.to(cuda_device), fmt_name)
+    q, s = q.cpu().numpy(), np.float32(s.item())
+    # the scale: IEEE quotient within 1 ulp (exact equality with the reference is checked below)
+    ieee = fp8.scale_from_amax(fp8.amax_f16(x.numpy()), fmt)
+    if np.isfinite(ieee):
+        assert abs(int(s.view(np.int32)) - int(ieee.view(np.int32))) <= 1, (s, ieee)
+    else:
+        assert s == ieee
+    # the bytes: exactly the oracle's element rule for that scale
+    q_ref = fp8.quantise_with_scale(x.numpy(), s, fmt)
+    assert np.array_equal(q, q_ref), f"{np.count_nonzero(q != q_ref)} bytes differ"
+
+
+@pytest.mark.parametrize("fmt_name", ["e4m3", "e5m2"])
+def test_dequantise_bit_exact(cuda_device, fmt_name):
+    fmt = fp8.FMT_NAMES[fmt_name]
+    codes = torch.arange(256, dtype=torch.uint8).repeat(41)[:10001]  # ragged, every code
+    for scale in (1.0, 0.0123, 146.2, 3.3e-9):
+        out = ops.dequantise(codes.to(cuda_device), scale, [codes.numel()], fmt_name).cpu().numpy()
+        ref = fp8.dequantise(codes.numpy(), scale, fmt)
+        # NaN payloads may differ between the GPU and numpy; NaN positions and every other bit must not
+        nan = np.isnan(ref)
+        assert np.array_equal(np.isnan(out), nan)
+        assert np.array_equal(out[~nan].view(np.uint16), ref[~nan].view(np.uint16))
+
+
+def test_scale_stays_on_device_and_matches_host_api(cuda_device):
+    import whisper_blaze_kernels as K
+    x = randn_f16((512, 512), 110).to(cuda_device)
+    q_host, s_host = K.quantise_e4m3(x)
+    q_dev, s_dev = K.quantise_e4m3_dev(x)
+    assert isinstance(s_host, float) and s_dev.is_cuda and s_dev.dtype == torch.float32
+    assert torch.equal(q_host, q_dev) and np.float32(s_host) == np.float32(s_dev.item())
+
+
+# ---- the reference's own quantiser tests (tests/test_kernels.py:42-79) on the B200 kernels
+
+def test_ref_suite_roundtrips(cuda_device):
+    import whisper_blaze_kernels as K
+    x = torch.randn(128, 512, dtype=torch.float16, device=cuda_device)
+    fp, scale = K.quantise_e4m3(x)
+    assert fp.shape == x.shape and scale > 0
+    x = torch.randn(512, 512, dtype=torch.float16, device=cuda_device)
+    fp, scale = K.quantise_e4m3(x)
+    xh = K.dequantise_e4m3(fp, scale, list(x.shape))
+    assert torch.allclose(x.float(), xh.float(), atol=0.1, rtol=0.2)
+    fp, scale = K.quantise_e5m2(x)
+    xh = K.dequantise_e5m2(fp, scale, list(x.shape))
+    assert torch.allclose(x.float(), xh.float(), atol=0.2, rtol=0.3)
+    z = torch.zeros(64, 64, dtype=torch.float16, device=cuda_device)
+    fp, scale = K.quantise_e4m3(z)
+    assert torch.allclose(K.dequantise_e4m3(fp, scale, [64, 64]).float(), z.float(), atol=1e-6)
+
+
+def test_dequantise_shape_mismatch_raises(cuda_device):
+    import whisper_blaze_kernels as K
+    fp, s = K.quantise_e4m3(torch.randn(8, 8, dtype=torch.float16, device=cuda_device))
+    with pytest.raises(RuntimeError, match="holds"):
+        K.dequantise_e4m3(fp, s, [8, 9])
+
+
+# ---- against the reference scale, every positive finite fp16 amax
+
+def _our_scale_table(cuda_device, amax_bits: np.ndarray, fmt: int) -> np.ndarray:
+    L = _lib.lib()
+    n = len(amax_bits)
+    amax = torch.from_numpy(amax_bits.astype(np.int32)).to(cuda_device)
+    scales = torch.zeros(n, dtype=torch.float32, device=cuda_device)
+    dummy = torch.zeros(8, dtype=torch.float16, device=cuda_device)
+    dq = torch.zeros(8, dtype=torch.uint8, device=cuda_device)
+    stream = _lib.stream_of(dummy)
+    a0, s0 = amax.data_ptr(), scales.data_ptr()
+    for i in range(n):  # n == 0: only the scale is produced
+        _lib.check(L.wbk_quantise_from_amax_f16(dummy.data_ptr(), 0, fmt, a0 + 4 * i, dq.data_ptr(), s0 + 4 * i,
+                                                stream), "scale table")
+    return scales.cpu().numpy()
+
+
+def test_scale_table_matches_reference_golden(cuda_device):
+    path = os.path.join(GOLDEN_DIR, "ref_scale_table.npz")
+    if not os.path.exists(path):
+        pytest.fail(f"{path} missing (generate with tests/golden/make_golden.py)")
+    g = np.load(path)
+    bits = g["amax_bits"].astype(np.uint16)
+    for fmt_name, fmt in fp8.FMT_NAMES.items():
+        ours = _our_scale_table(cuda_device, bits, fmt)
+        ref = g[f"scale_{fmt_name}"].astype(np.float32)
+        bad = np.flatnonzero(ours.view(np.int32) != ref.view(np.int32))
+        assert bad.size == 0, f"{fmt_name}: {bad.size} scales differ from the reference, e.g. amax bits {bits[bad[:5]]}"
+
+
+def test_quantise_matches_reference_golden_bytes(cuda_device):
+    path = os.path.join(GOLDEN_DIR, "ref_quantise.npz")
+    if not os.path.exists(path):
+        pytest.fail(f"{path} missing (generate with tests/golden/make_golden.py)")
+    g = np.load(path)
+    for name in sorted({k.split("__")[0] for k in g.files}):
+        x = torch.from_numpy(g[f"{name}__x"])
+        for fmt_name in ("e4m3", "e5m2"):
+            q, s = ops.quantise(x.to(cuda_device), fmt_name)
+            assert np.array_equal(q.cpu().numpy(), g[f"{name}__q_{fmt_name}"]), f"{name} {fmt_name} bytes"
+            assert np.float32(s.item()).view(np.int32) == np.float32(g[f"{name}__s_{fmt_name}"]).view(np.int32)
+
+
+def _ref_module():
+    from oracle import build_ref
+    try:
+        return build_ref.load()
+    except ImportError as e:
+        pytest.skip(str(e))
+
+
+@pytest.mark.parametrize("name,x", [c for c in CASES if c[1].numel() % 8 == 0],
+                         ids=[c[0] for c in CASES if c[1].numel() % 8 == 0])
+def test_quantise_matches_live_reference_kernel(cuda_device, name, x):
+    """Same input through the reference's own CUDA quantiser (oracle/_ref) and ours."""
+    R = _ref_module()
+    xd = x.to(cuda_device).contiguous()
+    for fmt_name, ref_fn in (("e4m3", R.quantise_e4m3), ("e5m2", R.quantise_e5m2)):
+        q_ref, s_ref = ref_fn(xd)
+        q, s = ops.quantise(xd, fmt_name)
+        assert np.float32(s.item()).view(np.int32) == np.float32(s_ref).view(np.int32), (fmt_name, s.item(), s_ref)
+        assert torch.equal(q.cpu(), q_ref.cpu()), f"{fmt_name}: bytes differ from the reference kernel"

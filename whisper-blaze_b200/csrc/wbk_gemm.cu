@@ -1,0 +1,660 @@
+// FP8 x FP8 -> FP32 (TMEM) -> FP16 per-tensor-scaled GEMM on B200 tcgen05.
+//
+//   out[M,N] = epilogue((A[M,K] . W[N,K]^T) * descale + bias ...)
+//
+// The reference has no working FP8 GEMM: its Hopper wgmma kernel
+// (csrc/kernels/gemm_hopper.cu:179-269) is unbound, and BlazeLinear.forward
+// (whisper_blaze/model.py:80-109) dequantises both operands and calls an fp16
+// F.linear. This kernel computes what that path means — descale = a_scale *
+// w_scale applied to an fp32 accumulator, then bias, then fp16 (the intent of
+// gemm_hopper.cu:251-268) — natively on 5th-generation tensor cores:
+//
+//   * persistent grid, one CTA per SM, static round-robin over 128x256 tiles
+//     (N-fastest so consecutive CTAs share the A row-block in L2);
+//   * warp 0: TMA producer. A [128 x 128 B] and W [256 x 128 B] boxes, 128-byte
+//     swizzle, into a 4-stage shared-memory ring (48 KB per stage);
+//   * warp 1: TMEM owner + single-thread tcgen05.mma issuer
+//     (kind::f8f6f4, M=128 N=256 K=32, fp32 accumulate), committing each stage
+//     back to the producer and each finished tile to the epilogue;
+//   * warps 2-5: epilogue. Two 256-column fp32 accumulators in TMEM (all 512
+//     columns) so the epilogue of tile i overlaps the MMAs of tile i+1; each
+//     warp drains its 32 TMEM lanes with tcgen05.ld, applies descale, bias,
+//     exact-erf GELU or residual add (+ optional fp16 clamp), rounds to fp16,
+//     stores, and tracks max|out| for a fused per-tensor amax.
+//
+// Every mbarrier wait is bounded (wall-clock limit via %globaltimer): a wait
+// that runs out records WBK_ERR_DEVICE_TIMEOUT in a device word, raises a
+// CTA-wide abort flag so the other roles stop, drains its in-flight work with
+// bounded waits, releases TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdlib>
+#include <mutex>
+#include <vector>
+
+#include "wbk_common.cuh"
+
+namespace wbk {
+
+__device__ uint32_t g_device_error;  // first device-side error: code | site << 8
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 128;  // bytes of K per stage = fp8 elements = one 128-byte swizzle row
+constexpr int UMMA_K = 32;
+constexpr int STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * BK;  // 16 KB
+constexpr int B_STAGE_BYTES = BN * BK;  // 32 KB
+constexpr int NUM_ACC = 2;
+constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
+constexpr int THREADS = 192;
+
+enum : uint32_t {
+  SITE_PRODUCER_EMPTY = 1,
+  SITE_MMA_ACC_EMPTY = 2,
+  SITE_MMA_FULL = 3,
+  SITE_EPI_ACC_FULL = 4,
+  SITE_DRAIN = 5,
+  SITE_SELFTEST = 15,
+};
+
+struct SharedStorage {
+  uint8_t a[STAGES][A_STAGE_BYTES];  // 1024-byte aligned (swizzle atom)
+  uint8_t b[STAGES][B_STAGE_BYTES];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t acc_full[NUM_ACC];
+  uint64_t acc_empty[NUM_ACC];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+constexpr size_t SMEM_BYTES = sizeof(SharedStorage) + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+
+struct Params {
+  int M, N, K;
+  int tiles_n, num_tiles, kblocks;
+  float alpha;
+  const float* a_scale;
+  const float* w_scale;
+  const __half* bias;
+  const __half* residual;
+  __half* out;
+  uint32_t* out_amax;
+  uint32_t idesc;
+  uint64_t timeout_ns;
+};
+
+// ------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void record_device_error(uint32_t code, uint32_t site) {
+  atomicCAS(&g_device_error, 0u, code | (site << 8));
+}
+
+// Bounded wait: true when the phase with `parity` completed; false when the
+// CTA abort flag is raised or `timeout_ns` of wall clock passed (the latter
+// records the error and raises the abort flag). Iterations are capped too.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                            uint64_t timeout_ns, uint32_t site) {
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0; it < (1u << 30); ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15u) == 15u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > timeout_ns) break;
+    }
+  }
+  record_device_error(WBK_ERR_DEVICE_TIMEOUT, site);
+  *abort_flag = 1;
+  return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t timeout_ns, uint32_t site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag, timeout_ns, site);
+}
+
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] . B[smem]^T, one 128x256x32 fp8 MMA, issued by one thread.
+__device__ __forceinline__ void umma_f8f6f4(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  const uint32_t m0 = 0, m1 = 0, m2 = 0, m3 = 0;  // no disabled output lanes
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(m0), "r"(m1), "r"(m2), "r"(m3)
+      : "memory");
+}
+
+// Arrive once on `bar` when every tcgen05 op issued so far by this thread is done.
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: thread i gets lane (base+i).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major operand tile written by TMA
+// with 128-byte swizzle: rows of 128 bytes, 8-row (1024-byte) swizzle atoms
+// stacked along M/N. Fields: start address >> 4 [0,14); leading-dimension
+// byte offset >> 4 [16,30) (unused for swizzled K-major, set to 1);
+// stride-dimension byte offset >> 4 [32,46) = 1024 B between 8-row groups;
+// descriptor version 1 [46,48); base offset 0; swizzle mode 2 = 128B [61,64).
+__device__ __forceinline__ uint64_t make_sw128_desc(const void* smem_ptr) {
+  const uint32_t addr = smem_u32(smem_ptr);
+  uint64_t d = static_cast<uint64_t>((addr & 0x3FFFFu) >> 4);
+  d |= static_cast<uint64_t>(1) << 16;
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// ----------------------------------------------------------------- epilogue
+
+template <int kEpi>
+__device__ __forceinline__ float epi_apply(float v) {
+  if (kEpi == WBK_EPI_GELU) v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
+  return v;
+}
+
+// Processes one 32-column chunk of one row (this thread's row) and stores it.
+template <int kEpi, bool kVec>
+__device__ __forceinline__ uint32_t epi_chunk(const Params& p, const uint32_t* acc, int row, int col0, float descale) {
+  const int N = p.N;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]) * descale;
+  const bool full = kVec && (col0 + 32 <= N);
+  if (p.bias != nullptr) {
+    if (full) {
+      const uint4* bv = reinterpret_cast<const uint4*>(p.bias + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 b = __ldg(bv + q);
+        const __half2* h = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 f = __half22float2(h[t]);
+          v[q * 8 + 2 * t] += f.x;
+          v[q * 8 + 2 * t + 1] += f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] += __half2float(p.bias[col0 + j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = epi_apply<kEpi>(v[j]);
+  if (kEpi == WBK_EPI_RESIDUAL || kEpi == WBK_EPI_RESIDUAL_CLAMP) {
+    const __half* rrow = p.residual + static_cast<int64_t>(row) * N;
+    if (full) {
+      const uint4* rv = reinterpret_cast<const uint4*>(rrow + col0);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 r = __ldg(rv + q);
+        const __half2* h = reinterpret_cast<const __half2*>(&r);
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const float2 f = __half22float2(h[t]);
+          v[q * 8 + 2 * t] += f.x;
+          v[q * 8 + 2 * t + 1] += f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) v[j] += __half2float(rrow[col0 + j]);
+    }
+    if (kEpi == WBK_EPI_RESIDUAL_CLAMP) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = fminf(fmaxf(v[j], -64504.0f), 64504.0f);
+    }
+  }
+  __half* orow = p.out + static_cast<int64_t>(row) * N;
+  uint32_t m = 0;
+  if (full) {
+    uint4* ov = reinterpret_cast<uint4*>(orow + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 o;
+      uint32_t* w = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const __half2 h = __halves2half2(__float2half_rn(v[q * 8 + 2 * t]), __float2half_rn(v[q * 8 + 2 * t + 1]));
+        w[t] = *reinterpret_cast<const uint32_t*>(&h);
+        m = __vmaxu2(m, abs2_nonan(w[t]));
+      }
+      ov[q] = o;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      if (col0 + j < N) {
+        const __half h = __float2half_rn(v[j]);
+        orow[col0 + j] = h;
+        m = __vmaxu2(m, abs2_nonan(__half_as_ushort(h)));
+      }
+    }
+  }
+  return max(m & 0xFFFFu, m >> 16);
+}
+
+// ------------------------------------------------------------------- kernel
+
+template <int kEpi, bool kVec>
+__global__ void __launch_bounds__(THREADS, 1)
+fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
+                const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  SharedStorage& s =
+      *reinterpret_cast<SharedStorage*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int* abort_flag = &s.abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int i = 0; i < NUM_ACC; ++i) {
+      mbar_init(&s.acc_full[i], 1);
+      mbar_init(&s.acc_empty[i], 4);  // one arrival per epilogue warp
+    }
+    mbar_init(&s.drain, 1);
+    s.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    prefetch_tmap(&tmap_a);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / p.tiles_n) * BM;
+        const int n0 = (tile % p.tiles_n) * BN;
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.full[stage], A_STAGE_BYTES + B_STAGE_BYTES);
+          tma_load_2d(&tmap_a, &s.full[stage], s.a[stage], kb * BK, m0);
+          tma_load_2d(&tmap_w, &s.full[stage], s.b[stage], kb * BK, n0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (ok) {
+        // Producer tail: wait until the MMA warp has released every stage, so
+        // no tcgen05.commit arrival to this CTA's barriers is still in flight
+        // when it exits.
+        for (int i = 0; i < STAGES; ++i) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) break;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      } else {
+        // Abort path: let the copies already issued land before the CTA exits.
+        // Stage i was last filled with phase (phase if i < stage else phase^1).
+        for (int i = 0; i < STAGES; ++i) {
+          const uint32_t ph = (i < stage) ? phase : (phase ^ 1u);
+          int dummy = 0;
+          mbar_wait(&s.full[i], ph, &dummy, 1000000ull, SITE_DRAIN);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1u, abort_flag, p.timeout_ns, SITE_MMA_ACC_EMPTY)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.kblocks; ++kb) {
+          if (!mbar_wait(&s.full[stage], phase, abort_flag, p.timeout_ns, SITE_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = make_sw128_desc(s.a[stage]);
+          const uint64_t bdesc = make_sw128_desc(s.b[stage]);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            // Advance the start address by k*32 bytes inside the 128-byte swizzle row.
+            const uint64_t koff = static_cast<uint64_t>((k * UMMA_K) >> 4);
+            umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(&s.empty[stage]);  // frees this smem stage once its MMAs retire
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&s.acc_full[acc]);  // accumulator ready for the epilogue
+        if (++acc == NUM_ACC) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        // Abort path: wait for every MMA this thread issued before TMEM is freed.
+        umma_commit(&s.drain);
+        int dummy = 0;
+        mbar_wait(&s.drain, 0, &dummy, 1000000ull, SITE_DRAIN);
+      }
+    }
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int quarter = warp & 3;  // TMEM lanes this warp may access: 32*quarter ..
+    const float descale = p.alpha * (p.a_scale ? __ldg(p.a_scale) : 1.0f) * (p.w_scale ? __ldg(p.w_scale) : 1.0f);
+    uint32_t amax = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      if (!mbar_wait(&s.acc_full[acc], acc_phase, abort_flag, p.timeout_ns, SITE_EPI_ACC_FULL)) break;
+      tc_fence_after();
+      const int m0 = (tile / p.tiles_n) * BM;
+      const int n0 = (tile % p.tiles_n) * BN;
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        if (n0 + c >= p.N) break;  // warp-uniform
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c), r);
+        tmem_ld_wait();
+        if (row < p.M) amax = max(amax, epi_chunk<kEpi, kVec>(p, r, row, n0 + c, descale));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
+      if (++acc == NUM_ACC) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (p.out_amax != nullptr) {
+      amax = warp_max_u32(amax);
+      if (lane == 0 && amax != 0u) atomicMax(p.out_amax, amax);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+__global__ void selftest_wait_kernel(uint64_t timeout_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&bar, 0, &abort_flag, timeout_ns, SITE_SELFTEST);  // nothing ever arrives
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------- host
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static std::once_flag once;
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+// 2-D uint8 tensor map: inner dim K (contiguous), outer dim rows, 128B swizzle.
+int make_tmap(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows, uint32_t box_rows) {
+  auto encode = get_encode_fn();
+  if (encode == nullptr) return fail(WBK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const cuuint64_t dims[2] = {k, rows};
+  const cuuint64_t strides[1] = {k};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(WBK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return WBK_OK;
+}
+
+uint64_t wait_timeout_ns() {
+  static uint64_t t = [] {
+    const char* e = std::getenv("WBK_WAIT_TIMEOUT_MS");
+    const long long ms = e ? std::atoll(e) : 0;
+    return static_cast<uint64_t>(ms > 0 ? ms : 4000) * 1000000ull;
+  }();
+  return t;
+}
+
+template <int kEpi, bool kVec>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const Params& p, int grid, cudaStream_t stream) {
+  static std::mutex mu;
+  static std::vector<char> configured;
+  const int dev = current_device();
+  if (dev < 0) return fail(WBK_ERR_CUDA, "no current CUDA device");
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
+    if (!configured[dev]) {
+      if (int e = cuda_check(cudaFuncSetAttribute(fp8_gemm_kernel<kEpi, kVec>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(SMEM_BYTES)),
+                             "cudaFuncSetAttribute(max dynamic smem)"))
+        return e;
+      configured[dev] = 1;
+    }
+  }
+  fp8_gemm_kernel<kEpi, kVec><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tw, p);
+  return cuda_check(cudaGetLastError(), "fp8 gemm launch");
+}
+
+template <int kEpi>
+int dispatch_vec(bool vec, const CUtensorMap& ta, const CUtensorMap& tw, const Params& p, int grid, cudaStream_t s) {
+  return vec ? launch_gemm<kEpi, true>(ta, tw, p, grid, s) : launch_gemm<kEpi, false>(ta, tw, p, grid, s);
+}
+
+}  // namespace
+}  // namespace wbk
+
+using namespace wbk;
+
+extern "C" {
+
+int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int a_fmt, int w_fmt, float alpha,
+                 const float* a_scale, const float* w_scale, const void* bias, const void* residual, void* out,
+                 int epilogue, uint32_t* out_amax_bits, wbk_stream_t stream) {
+  if (M < 0 || N <= 0 || K <= 0)
+    return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
+                (long long)K);
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || M * N > (int64_t(1) << 46))
+    return fail(WBK_ERR_UNSUPPORTED, "wbk_gemm_fp8: shape too large");
+  if (K % 16 != 0) return fail(WBK_ERR_UNSUPPORTED, "wbk_gemm_fp8: K=%lld must be a multiple of 16 (TMA row pitch)", (long long)K);
+  if ((a_fmt != WBK_FMT_E4M3 && a_fmt != WBK_FMT_E5M2) || (w_fmt != WBK_FMT_E4M3 && w_fmt != WBK_FMT_E5M2))
+    return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: unknown fp8 format");
+  if (epilogue < WBK_EPI_NONE || epilogue > WBK_EPI_RESIDUAL_CLAMP)
+    return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: unknown epilogue %d", epilogue);
+  const bool needs_res = epilogue == WBK_EPI_RESIDUAL || epilogue == WBK_EPI_RESIDUAL_CLAMP;
+  if (needs_res && residual == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: residual epilogue without residual");
+  if (M == 0) return WBK_OK;
+  if (A == nullptr || W == nullptr || out == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: null pointer");
+  if (!aligned(A, 16) || !aligned(W, 16)) return fail(WBK_ERR_UNSUPPORTED, "wbk_gemm_fp8: A and W must be 16-byte aligned");
+  if (!aligned(out, 2) || (bias && !aligned(bias, 2)) || (residual && !aligned(residual, 2)))
+    return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: fp16 pointers must be 2-byte aligned");
+
+  CUtensorMap ta, tw;
+  if (int e = make_tmap(&ta, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), BM)) return e;
+  if (int e = make_tmap(&tw, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BN)) return e;
+
+  Params p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  const int tiles_m = static_cast<int>((M + BM - 1) / BM);
+  p.tiles_n = static_cast<int>((N + BN - 1) / BN);
+  const int64_t num_tiles = static_cast<int64_t>(tiles_m) * p.tiles_n;
+  if (num_tiles > INT32_MAX) return fail(WBK_ERR_UNSUPPORTED, "wbk_gemm_fp8: too many tiles");
+  p.num_tiles = static_cast<int>(num_tiles);
+  p.kblocks = static_cast<int>((K + BK - 1) / BK);
+  p.alpha = alpha;
+  p.a_scale = a_scale;
+  p.w_scale = w_scale;
+  p.bias = static_cast<const __half*>(bias);
+  p.residual = static_cast<const __half*>(residual);
+  p.out = static_cast<__half*>(out);
+  p.out_amax = out_amax_bits;
+  // Instruction descriptor (kind::f8f6f4): D fp32 [4,6)=1; A format [7,10);
+  // B format [10,13); both K-major (bits 15,16 = 0); N>>3 [17,23); M>>4 [24,29).
+  p.idesc = (1u << 4) | (static_cast<uint32_t>(a_fmt) << 7) | (static_cast<uint32_t>(w_fmt) << 10) |
+            (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+  p.timeout_ns = wait_timeout_ns();
+
+  const bool vec = (N % 8 == 0) && aligned(out, 16) && (!bias || aligned(bias, 16)) && (!residual || aligned(residual, 16));
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int grid = static_cast<int>(num_tiles < sms ? num_tiles : sms);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  switch (epilogue) {
+    case WBK_EPI_NONE: return dispatch_vec<WBK_EPI_NONE>(vec, ta, tw, p, grid, s);
+    case WBK_EPI_GELU: return dispatch_vec<WBK_EPI_GELU>(vec, ta, tw, p, grid, s);
+    case WBK_EPI_RESIDUAL: return dispatch_vec<WBK_EPI_RESIDUAL>(vec, ta, tw, p, grid, s);
+    default: return dispatch_vec<WBK_EPI_RESIDUAL_CLAMP>(vec, ta, tw, p, grid, s);
+  }
+}
+
+int wbk_device_error(uint32_t* code_out) {
+  if (code_out == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_device_error: null pointer");
+  if (int e = cuda_check(cudaDeviceSynchronize(), "wbk_device_error synchronize")) return e;
+  uint32_t v = 0;
+  if (int e = cuda_check(cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v)), "wbk_device_error read")) return e;
+  const uint32_t zero = 0;
+  if (int e = cuda_check(cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero)), "wbk_device_error clear")) return e;
+  *code_out = v;
+  return WBK_OK;
+}
+
+int wbk_selftest_bounded_wait(uint64_t timeout_ns, wbk_stream_t stream) {
+  if (timeout_ns == 0 || timeout_ns > 10ull * 1000000000ull)
+    return fail(WBK_ERR_INVALID_ARG, "wbk_selftest_bounded_wait: timeout must be in (0, 10 s]");
+  selftest_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(timeout_ns);
+  return cuda_check(cudaGetLastError(), "selftest launch");
+}
+
+}  // extern "C"

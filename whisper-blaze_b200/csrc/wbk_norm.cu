@@ -1,0 +1,301 @@
+// Fused residual-add + LayerNorm / RMSNorm for B200.
+//
+// Semantics follow the reference's layernorm_fused_kernel and
+// rmsnorm_fused_kernel (csrc/kernels/layernorm_fused.cu:50-184, :191-258):
+// s = float(x) (+ float(residual)); mean and variance in fp32 (two passes over
+// the row, the second over (s - mean)); out = fp16((s - mean) * rsqrt(var + eps)
+// * gamma + beta); the optional sum output is fp16(s).
+//
+// Design: one warp per row with the whole row held in registers (D <= 4096),
+// so x and residual are read from HBM exactly once — the reference reads them
+// three times, one CTA per row. Rows are strided over a persistent grid so the
+// optional output-amax (for a following FP8 quantise without another pass)
+// costs one atomic per CTA. Rows with D > 4096 use a CTA-per-row kernel that
+// re-reads the row (served from L2).
+#include "wbk_common.cuh"
+
+namespace wbk {
+namespace {
+
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+
+__device__ __forceinline__ void unpack8(const uint4& v, float* f) {
+  const __half2* h = reinterpret_cast<const __half2*>(&v);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 t = __half22float2(h[j]);
+    f[2 * j] = t.x;
+    f[2 * j + 1] = t.y;
+  }
+}
+
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 r;
+  uint32_t* w = reinterpret_cast<uint32_t*>(&r);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const __half2 h = __halves2half2(__float2half_rn(f[2 * j]), __float2half_rn(f[2 * j + 1]));
+    w[j] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return r;
+}
+
+__device__ __forceinline__ uint32_t amax8(const uint4& v) {
+  const uint32_t m = __vmaxu2(__vmaxu2(abs2_nonan(v.x), abs2_nonan(v.y)), __vmaxu2(abs2_nonan(v.z), abs2_nonan(v.w)));
+  return max(m & 0xFFFFu, m >> 16);
+}
+
+__device__ __forceinline__ void block_amax_commit(uint32_t m, uint32_t* out_amax) {
+  __shared__ uint32_t red[kWarps];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  m = warp_max_u32(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    m = lane < kWarps ? red[lane] : 0u;
+    m = warp_max_u32(m);
+    if (lane == 0 && m != 0u) atomicMax(out_amax, m);
+  }
+}
+
+// kVpl = 16-byte vectors (8 halves) per lane; the row has D/8 vectors.
+template <int kVpl, bool kRms>
+__global__ void __launch_bounds__(kThreads)
+norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, const __half* __restrict__ gamma,
+                 const __half* __restrict__ beta, __half* __restrict__ out, __half* __restrict__ sum_out,
+                 int64_t rows, int D, float eps, uint32_t* __restrict__ out_amax) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = D >> 3;
+  const float fD = static_cast<float>(D);
+  uint32_t amax = 0;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp; row < rows;
+       row += static_cast<int64_t>(gridDim.x) * kWarps) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * D);
+    const uint4* rr = res ? reinterpret_cast<const uint4*>(res + row * D) : nullptr;
+    float v[kVpl][8];
+    float s = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kVpl; ++i) {
+      const int idx = lane + 32 * i;
+      if (idx < nvec) {
+        unpack8(ld_stream16(xr + idx), v[i]);
+        if (rr) {
+          float r8[8];
+          unpack8(ld_stream16(rr + idx), r8);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[i][j] += r8[j];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += kRms ? v[i][j] * v[i][j] : v[i][j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+      }
+    }
+    s = warp_sum(s);
+    float mean = 0.0f, inv;
+    if (kRms) {
+      inv = rsqrtf(s / fD + eps);
+    } else {
+      mean = s / fD;
+      float var = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kVpl; ++i) {
+        if (lane + 32 * i < nvec) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const float d = v[i][j] - mean;
+            var += d * d;
+          }
+        }
+      }
+      var = warp_sum(var);
+      inv = rsqrtf(var / fD + eps);
+    }
+    uint4* orow = reinterpret_cast<uint4*>(out + row * D);
+    uint4* srow = sum_out ? reinterpret_cast<uint4*>(sum_out + row * D) : nullptr;
+#pragma unroll
+    for (int i = 0; i < kVpl; ++i) {
+      const int idx = lane + 32 * i;
+      if (idx < nvec) {
+        float g[8], o[8];
+        unpack8(__ldg(reinterpret_cast<const uint4*>(gamma) + idx), g);
+        if (kRms) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = (v[i][j] * inv) * g[j];
+        } else {
+          float b[8];
+          unpack8(__ldg(reinterpret_cast<const uint4*>(beta) + idx), b);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = ((v[i][j] - mean) * inv) * g[j] + b[j];
+        }
+        const uint4 ov = pack8(o);
+        orow[idx] = ov;
+        if (out_amax) amax = max(amax, amax8(ov));
+        if (srow) srow[idx] = pack8(v[i]);
+      }
+    }
+  }
+  if (out_amax) block_amax_commit(amax, out_amax);
+}
+
+// CTA per row, for D > 32*8*16. Three reads of the row (L2-resident).
+template <bool kRms>
+__global__ void __launch_bounds__(kThreads)
+norm_block_kernel(const __half* __restrict__ x, const __half* __restrict__ res, const __half* __restrict__ gamma,
+                  const __half* __restrict__ beta, __half* __restrict__ out, __half* __restrict__ sum_out,
+                  int64_t rows, int D, float eps, uint32_t* __restrict__ out_amax) {
+  __shared__ float red[kWarps];
+  __shared__ float bcast;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = D >> 3;
+  const float fD = static_cast<float>(D);
+  uint32_t amax = 0;
+  auto block_sum = [&](float v) -> float {
+    v = warp_sum(v);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    if (warp == 0) {
+      v = lane < kWarps ? red[lane] : 0.0f;
+      v = warp_sum(v);
+      if (lane == 0) bcast = v;
+    }
+    __syncthreads();
+    const float r = bcast;
+    __syncthreads();  // red/bcast are reused by the next reduction
+    return r;
+  };
+  for (int64_t row = blockIdx.x; row < rows; row += gridDim.x) {
+    const uint4* xr = reinterpret_cast<const uint4*>(x + row * D);
+    const uint4* rr = res ? reinterpret_cast<const uint4*>(res + row * D) : nullptr;
+    auto load = [&](int idx, float* f) {
+      unpack8(xr[idx], f);
+      if (rr) {
+        float r8[8];
+        unpack8(rr[idx], r8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] += r8[j];
+      }
+    };
+    float s = 0.0f;
+    for (int idx = threadIdx.x; idx < nvec; idx += kThreads) {
+      float f[8];
+      load(idx, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += kRms ? f[j] * f[j] : f[j];
+    }
+    s = block_sum(s);
+    float mean = 0.0f, inv;
+    if (kRms) {
+      inv = rsqrtf(s / fD + eps);
+    } else {
+      mean = s / fD;
+      float var = 0.0f;
+      for (int idx = threadIdx.x; idx < nvec; idx += kThreads) {
+        float f[8];
+        load(idx, f);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float d = f[j] - mean;
+          var += d * d;
+        }
+      }
+      var = block_sum(var);
+      inv = rsqrtf(var / fD + eps);
+    }
+    for (int idx = threadIdx.x; idx < nvec; idx += kThreads) {
+      float f[8], g[8], o[8];
+      load(idx, f);
+      unpack8(reinterpret_cast<const uint4*>(gamma)[idx], g);
+      if (kRms) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = (f[j] * inv) * g[j];
+      } else {
+        float b[8];
+        unpack8(reinterpret_cast<const uint4*>(beta)[idx], b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = ((f[j] - mean) * inv) * g[j] + b[j];
+      }
+      const uint4 ov = pack8(o);
+      reinterpret_cast<uint4*>(out + row * D)[idx] = ov;
+      if (out_amax) amax = max(amax, amax8(ov));
+      if (sum_out) reinterpret_cast<uint4*>(sum_out + row * D)[idx] = pack8(f);
+    }
+  }
+  if (out_amax) block_amax_commit(amax, out_amax);
+}
+
+template <bool kRms>
+int launch_norm(const void* x, const void* res, const void* gamma, const void* beta, void* out, void* sum_out,
+                int64_t rows, int64_t D, float eps, uint32_t* out_amax, cudaStream_t s) {
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* rh = static_cast<const __half*>(res);
+  const __half* gh = static_cast<const __half*>(gamma);
+  const __half* bh = static_cast<const __half*>(beta);
+  __half* oh = static_cast<__half*>(out);
+  __half* sh = static_cast<__half*>(sum_out);
+  const int d = static_cast<int>(D);
+  const int nvec = d / 8;
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t want = (rows + kWarps - 1) / kWarps;
+  const int grid = static_cast<int>(want < sms * 4 ? want : sms * 4);
+#define WBK_NORM_CASE(V)                                                                       \
+  if (nvec <= 32 * (V)) {                                                                      \
+    norm_warp_kernel<V, kRms><<<grid, kThreads, 0, s>>>(xh, rh, gh, bh, oh, sh, rows, d, eps, out_amax); \
+    return cuda_check(cudaGetLastError(), "norm kernel launch");                               \
+  }
+  WBK_NORM_CASE(1)
+  WBK_NORM_CASE(2)
+  WBK_NORM_CASE(3)
+  WBK_NORM_CASE(4)
+  WBK_NORM_CASE(5)
+  WBK_NORM_CASE(6)
+  WBK_NORM_CASE(8)
+  WBK_NORM_CASE(12)
+  WBK_NORM_CASE(16)
+#undef WBK_NORM_CASE
+  const int bgrid = static_cast<int>(rows < sms * 8 ? rows : sms * 8);
+  norm_block_kernel<kRms><<<bgrid, kThreads, 0, s>>>(xh, rh, gh, bh, oh, sh, rows, d, eps, out_amax);
+  return cuda_check(cudaGetLastError(), "norm kernel launch");
+}
+
+int check_norm_args(const char* who, const void* x, const void* res, const void* gamma, const void* beta, const void* out,
+                    const void* sum_out, int64_t rows, int64_t D, bool need_beta) {
+  if (rows < 0 || D <= 0) return fail(WBK_ERR_INVALID_ARG, "%s: rows=%lld D=%lld", who, (long long)rows, (long long)D);
+  if (D % 8 != 0) return fail(WBK_ERR_UNSUPPORTED, "%s: last dimension %lld is not a multiple of 8", who, (long long)D);
+  if (D > (int64_t(1) << 30)) return fail(WBK_ERR_UNSUPPORTED, "%s: last dimension too large", who);
+  if (x == nullptr || gamma == nullptr || out == nullptr || (need_beta && beta == nullptr))
+    return fail(WBK_ERR_INVALID_ARG, "%s: null pointer", who);
+  const void* ptrs[6] = {x, res, gamma, beta, out, sum_out};
+  for (const void* p : ptrs)
+    if (p != nullptr && !aligned(p, 16)) return fail(WBK_ERR_UNSUPPORTED, "%s: pointer %p is not 16-byte aligned", who, p);
+  return WBK_OK;
+}
+
+}  // namespace
+}  // namespace wbk
+
+using namespace wbk;
+
+extern "C" {
+
+int wbk_layernorm_f16(const void* x, const void* residual, const void* gamma, const void* beta, void* out,
+                      void* sum_out, int64_t rows, int64_t D, float eps, uint32_t* out_amax_bits,
+                      wbk_stream_t stream) {
+  if (int e = check_norm_args("wbk_layernorm_f16", x, residual, gamma, beta, out, sum_out, rows, D, true)) return e;
+  if (rows == 0) return WBK_OK;
+  return launch_norm<false>(x, residual, gamma, beta, out, sum_out, rows, D, eps, out_amax_bits,
+                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+int wbk_rmsnorm_f16(const void* x, const void* residual, const void* gamma, void* out, int64_t rows, int64_t D,
+                    float eps, wbk_stream_t stream) {
+  if (residual == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_rmsnorm_f16: residual is required");
+  if (int e = check_norm_args("wbk_rmsnorm_f16", x, residual, gamma, nullptr, out, nullptr, rows, D, false)) return e;
+  if (rows == 0) return WBK_OK;
+  return launch_norm<true>(x, residual, gamma, nullptr, out, nullptr, rows, D, eps, nullptr,
+                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,258 @@
+// Per-tensor FP8 (E4M3 / E5M2) amax, quantise and dequantise kernels for B200.
+//
+// This translation unit is compiled with --use_fast_math, the flag set the
+// reference builds its quantiser with (setup.py:41-54), so that the scale
+// expression `amax / max_fp8` (max_fp8 a runtime value) is evaluated by the
+// same compiler division as the reference's compute_scale_kernel
+// (csrc/kernels/fp8_quantize.cu:72). Everything else here is exact in either
+// mode: fp16->fp32 conversion, one fp32 multiply per element, fminf/fmaxf and
+// the hardware round-to-nearest-even, saturate-to-finite fp8 conversion.
+//
+// Layout in HBM: the input is a flat fp16 array (any shape, contiguous); the
+// output is a flat uint8 array of the same element count. Each thread moves
+// 8 elements per step: one 16-byte load in, one 8-byte store out.
+#include "wbk_common.cuh"
+
+namespace wbk {
+namespace {
+
+constexpr int kThreads = 256;
+
+__host__ __device__ constexpr float fmt_max(int fmt) { return fmt == WBK_FMT_E4M3 ? 448.0f : 57344.0f; }
+
+// -------------------------------------------------------------------- amax
+
+// Grid-stride max(|x|) over n fp16 values, NaN ignored, packed-fp16 integer
+// max (|x| as an unsigned bit pattern orders like the value for non-NaN).
+// One atomicMax per CTA into *amax_bits.
+template <bool kVec>
+__global__ void __launch_bounds__(kThreads)
+amax_f16_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ amax_bits) {
+  uint32_t m = 0;  // two packed running maxima
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (kVec) {
+    const int64_t nvec = n >> 3;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    int64_t i = tid;
+    for (; i + 3 * stride < nvec; i += 4 * stride) {
+      const uint4 v0 = ld_stream16(xv + i);
+      const uint4 v1 = ld_stream16(xv + i + stride);
+      const uint4 v2 = ld_stream16(xv + i + 2 * stride);
+      const uint4 v3 = ld_stream16(xv + i + 3 * stride);
+      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v0.x), abs2_nonan(v0.y)),
+                               __vmaxu2(abs2_nonan(v0.z), abs2_nonan(v0.w))));
+      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v1.x), abs2_nonan(v1.y)),
+                               __vmaxu2(abs2_nonan(v1.z), abs2_nonan(v1.w))));
+      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v2.x), abs2_nonan(v2.y)),
+                               __vmaxu2(abs2_nonan(v2.z), abs2_nonan(v2.w))));
+      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v3.x), abs2_nonan(v3.y)),
+                               __vmaxu2(abs2_nonan(v3.z), abs2_nonan(v3.w))));
+    }
+    for (; i < nvec; i += stride) {
+      const uint4 v = ld_stream16(xv + i);
+      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v.x), abs2_nonan(v.y)),
+                               __vmaxu2(abs2_nonan(v.z), abs2_nonan(v.w))));
+    }
+    done = nvec << 3;
+  }
+  const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
+  for (int64_t i = done + tid; i < n; i += stride) m = __vmaxu2(m, abs2_nonan(xs[i]));
+
+  uint32_t mm = max(m & 0xFFFFu, m >> 16);
+  mm = warp_max_u32(mm);
+  __shared__ uint32_t red[kThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = mm;
+  __syncthreads();
+  if (warp == 0) {
+    mm = lane < kThreads / 32 ? red[lane] : 0u;
+    mm = warp_max_u32(mm);
+    if (lane == 0 && mm != 0u) atomicMax(amax_bits, mm);
+  }
+}
+
+// ---------------------------------------------------------------- quantise
+
+// The reference's scale rule: scale = amax / max_fp8, replaced by 1.0 unless
+// it is > 0 (fp8_quantize.cu:72 and :218); inv_scale = 1/scale rounded to
+// nearest (host IEEE division at fp8_quantize.cu:224; __frcp_rn is the
+// correctly rounded reciprocal, so the two agree for every scale).
+__device__ __forceinline__ void scale_from_amax(uint32_t amax_bits, float max_fp8, float& scale, float& inv) {
+  const float amax = half_bits_to_float(amax_bits);
+  float s = amax / max_fp8;
+  s = (s > 0.0f) ? s : 1.0f;
+  scale = s;
+  inv = __frcp_rn(s);
+}
+
+template <int kFmt>
+__device__ __forceinline__ uint32_t q8x2(float a, float b, float inv, float mx) {
+  float2 f;
+  f.x = fminf(fmaxf(a * inv, -mx), mx);
+  f.y = fminf(fmaxf(b * inv, -mx), mx);
+  return __nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, kFmt == WBK_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2);
+}
+
+template <int kFmt>
+__device__ __forceinline__ uint32_t q8x4(uint32_t h01, uint32_t h23, float inv, float mx) {
+  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
+  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
+  return q8x2<kFmt>(f01.x, f01.y, inv, mx) | (q8x2<kFmt>(f23.x, f23.y, inv, mx) << 16);
+}
+
+template <int kFmt, bool kVec>
+__global__ void __launch_bounds__(kThreads)
+quantise_f16_kernel(const __half* __restrict__ x, int64_t n, const uint32_t* __restrict__ amax_bits,
+                    float max_fp8, uint8_t* __restrict__ q, float* __restrict__ scale_out) {
+  float scale, inv;
+  scale_from_amax(*amax_bits, max_fp8, scale, inv);
+  if (scale_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (kVec) {
+    const int64_t nvec = n >> 3;
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    uint2* qv = reinterpret_cast<uint2*>(q);
+    int64_t i = tid;
+    for (; i + stride < nvec; i += 2 * stride) {
+      const uint4 v0 = ld_stream16(xv + i);
+      const uint4 v1 = ld_stream16(xv + i + stride);
+      qv[i] = make_uint2(q8x4<kFmt>(v0.x, v0.y, inv, max_fp8), q8x4<kFmt>(v0.z, v0.w, inv, max_fp8));
+      qv[i + stride] = make_uint2(q8x4<kFmt>(v1.x, v1.y, inv, max_fp8), q8x4<kFmt>(v1.z, v1.w, inv, max_fp8));
+    }
+    for (; i < nvec; i += stride) {
+      const uint4 v = ld_stream16(xv + i);
+      qv[i] = make_uint2(q8x4<kFmt>(v.x, v.y, inv, max_fp8), q8x4<kFmt>(v.z, v.w, inv, max_fp8));
+    }
+    done = nvec << 3;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) {
+    const float f = __half2float(x[i]);
+    q[i] = static_cast<uint8_t>(q8x2<kFmt>(f, 0.0f, inv, max_fp8) & 0xFFu);
+  }
+}
+
+// -------------------------------------------------------------- dequantise
+
+template <int kFmt>
+__device__ __forceinline__ uint32_t dq8x2(uint32_t pair, float scale) {
+  const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(pair & 0xFFFFu),
+                                                    kFmt == WBK_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2);
+  const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+  const __half2 o = __halves2half2(__float2half_rn(f.x * scale), __float2half_rn(f.y * scale));
+  return *reinterpret_cast<const uint32_t*>(&o);
+}
+
+template <int kFmt, bool kVec>
+__global__ void __launch_bounds__(kThreads)
+dequantise_f16_kernel(const uint8_t* __restrict__ q, int64_t n, float scale, __half* __restrict__ out) {
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (kVec) {
+    const int64_t nvec = n >> 3;
+    const uint2* qv = reinterpret_cast<const uint2*>(q);
+    uint4* ov = reinterpret_cast<uint4*>(out);
+    for (int64_t i = tid; i < nvec; i += stride) {
+      const uint2 v = qv[i];
+      ov[i] = make_uint4(dq8x2<kFmt>(v.x, scale), dq8x2<kFmt>(v.x >> 16, scale),
+                         dq8x2<kFmt>(v.y, scale), dq8x2<kFmt>(v.y >> 16, scale));
+    }
+    done = nvec << 3;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) {
+    const uint32_t h = dq8x2<kFmt>(q[i], scale);
+    reinterpret_cast<unsigned short*>(out)[i] = static_cast<unsigned short>(h & 0xFFFFu);
+  }
+}
+
+int grid_for(int64_t work_items, int per_sm) {
+  const int64_t want = (work_items + kThreads - 1) / kThreads;
+  const int64_t cap = static_cast<int64_t>(sm_count() > 0 ? sm_count() : 148) * per_sm;
+  const int64_t g = want < 1 ? 1 : (want < cap ? want : cap);
+  return static_cast<int>(g);
+}
+
+int check_fmt(int fmt) {
+  if (fmt != WBK_FMT_E4M3 && fmt != WBK_FMT_E5M2) return fail(WBK_ERR_INVALID_ARG, "unknown fp8 format %d", fmt);
+  return WBK_OK;
+}
+
+}  // namespace
+}  // namespace wbk
+
+using namespace wbk;
+
+extern "C" {
+
+int wbk_amax_f16(const void* x, int64_t n, uint32_t* amax_bits, wbk_stream_t stream) {
+  if (n < 0) return fail(WBK_ERR_INVALID_ARG, "wbk_amax_f16: n < 0");
+  if (amax_bits == nullptr || (n > 0 && x == nullptr)) return fail(WBK_ERR_INVALID_ARG, "wbk_amax_f16: null pointer");
+  if (n == 0) return WBK_OK;
+  const bool vec = aligned(x, 16);
+  const int grid = grid_for(vec ? (n + 7) / 8 / 4 : n, 8);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (vec) amax_f16_kernel<true><<<grid, kThreads, 0, s>>>(static_cast<const __half*>(x), n, amax_bits);
+  else amax_f16_kernel<false><<<grid, kThreads, 0, s>>>(static_cast<const __half*>(x), n, amax_bits);
+  return cuda_check(cudaGetLastError(), "wbk_amax_f16 launch");
+}
+
+int wbk_quantise_from_amax_f16(const void* x, int64_t n, int fmt, const uint32_t* amax_bits, void* q_out,
+                               float* scale_out, wbk_stream_t stream) {
+  if (int e = check_fmt(fmt)) return e;
+  if (n < 0) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_from_amax_f16: n < 0");
+  if (amax_bits == nullptr || (n > 0 && (x == nullptr || q_out == nullptr)))
+    return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_from_amax_f16: null pointer");
+  const bool vec = aligned(x, 16) && aligned(q_out, 8);
+  const int grid = grid_for(vec ? (n + 7) / 8 / 2 : n, 16);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const float mx = fmt_max(fmt);
+  const __half* xh = static_cast<const __half*>(x);
+  uint8_t* q = static_cast<uint8_t*>(q_out);
+  if (fmt == WBK_FMT_E4M3) {
+    if (vec) quantise_f16_kernel<WBK_FMT_E4M3, true><<<grid, kThreads, 0, s>>>(xh, n, amax_bits, mx, q, scale_out);
+    else quantise_f16_kernel<WBK_FMT_E4M3, false><<<grid, kThreads, 0, s>>>(xh, n, amax_bits, mx, q, scale_out);
+  } else {
+    if (vec) quantise_f16_kernel<WBK_FMT_E5M2, true><<<grid, kThreads, 0, s>>>(xh, n, amax_bits, mx, q, scale_out);
+    else quantise_f16_kernel<WBK_FMT_E5M2, false><<<grid, kThreads, 0, s>>>(xh, n, amax_bits, mx, q, scale_out);
+  }
+  return cuda_check(cudaGetLastError(), "wbk_quantise_from_amax_f16 launch");
+}
+
+int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out, float* scale_out, uint32_t* amax_ws,
+                     wbk_stream_t stream) {
+  if (int e = check_fmt(fmt)) return e;
+  if (amax_ws == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_f16: amax_ws is null");
+  if (n < 0) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_f16: n < 0");
+  if (n > 0 && (x == nullptr || q_out == nullptr)) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_f16: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (int e = cuda_check(cudaMemsetAsync(amax_ws, 0, sizeof(uint32_t), s), "wbk_quantise_f16 memset")) return e;
+  if (int e = wbk_amax_f16(x, n, amax_ws, stream)) return e;
+  return wbk_quantise_from_amax_f16(x, n, fmt, amax_ws, q_out, scale_out, stream);
+}
+
+int wbk_dequantise_f16(const void* q, int64_t n, int fmt, float scale, void* out, wbk_stream_t stream) {
+  if (int e = check_fmt(fmt)) return e;
+  if (n < 0) return fail(WBK_ERR_INVALID_ARG, "wbk_dequantise_f16: n < 0");
+  if (n == 0) return WBK_OK;
+  if (q == nullptr || out == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_dequantise_f16: null pointer");
+  const bool vec = aligned(q, 8) && aligned(out, 16);
+  const int grid = grid_for(vec ? (n + 7) / 8 : n, 16);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const uint8_t* qq = static_cast<const uint8_t*>(q);
+  __half* o = static_cast<__half*>(out);
+  if (fmt == WBK_FMT_E4M3) {
+    if (vec) dequantise_f16_kernel<WBK_FMT_E4M3, true><<<grid, kThreads, 0, s>>>(qq, n, scale, o);
+    else dequantise_f16_kernel<WBK_FMT_E4M3, false><<<grid, kThreads, 0, s>>>(qq, n, scale, o);
+  } else {
+    if (vec) dequantise_f16_kernel<WBK_FMT_E5M2, true><<<grid, kThreads, 0, s>>>(qq, n, scale, o);
+    else dequantise_f16_kernel<WBK_FMT_E5M2, false><<<grid, kThreads, 0, s>>>(qq, n, scale, o);
+  }
+  return cuda_check(cudaGetLastError(), "wbk_dequantise_f16 launch");
+}
+
+}  // extern "C"

@@ -1,0 +1,243 @@
+"""Whisper-large-v3-shaped encoder stack with every linear in FP8 E4M3.
+
+Layer structure is HF WhisperEncoderLayer (pre-LN): LN -> self-attention ->
++residual -> LN -> fc1 -> GELU(erf) -> fc2 -> +residual -> fp16 clamp, then a
+final LayerNorm after the last layer. q/k/v are one fused [3*D, D] projection
+(k has no bias, so its third of the bias is zero). Attention is torch SDPA in
+fp16 (the reference's own attention: HF runs it through torch SDPA).
+
+Per layer, on one stream and without any host synchronisation:
+
+  LN1(h)            -> x   (fp16) + amax(x)            norm kernel
+  quantise(x)       -> xq  (fp8)  + scale              quantise kernel
+  QKV GEMM          -> qkv (fp16), bias epilogue       tcgen05 GEMM
+  SDPA(q, k, v)     -> a   (fp16)                      torch
+  amax+quantise(a)  -> aq  (fp8)                       2 kernels
+  out-proj GEMM     -> h2 = fp16(acc*s + b + h)        residual epilogue
+  LN2(h2)           -> x2  + amax(x2)                  norm kernel
+  quantise(x2)      -> x2q                             quantise kernel
+  fc1 GEMM          -> f = fp16(gelu(acc*s + b)) + amax(f)   GELU epilogue
+  quantise(f)       -> fq
+  fc2 GEMM          -> h' = fp16(clamp(acc*s + b + h2))      residual+clamp epilogue
+
+Activation scales live in device memory; weights are quantised once.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Callable, List, Optional
+
+import torch
+import torch.nn.functional as F
+
+from . import ops
+
+
+@dataclass
+class EncoderConfig:
+    d_model: int = 1280
+    heads: int = 20
+    ffn: int = 5120
+    layers: int = 32
+    seq_len: int = 1500
+    eps: float = 1e-5
+
+    @property
+    def head_dim(self) -> int:
+        return self.d_model // self.heads
+
+    def gemm_flops_per_token(self) -> int:
+        """FP8 GEMM FLOPs per token per layer (QKV + out-proj + fc1 + fc2)."""
+        D, Fd = self.d_model, self.ffn
+        return 2 * D * (3 * D + D + Fd) + 2 * Fd * D
+
+    def attn_flops_per_chunk(self) -> int:
+        """fp16 attention FLOPs per chunk per layer (QK^T and PV)."""
+        return 4 * self.seq_len * self.seq_len * self.d_model
+
+
+@dataclass
+class LayerWeights:
+    """fp16 master weights of one encoder layer (nn.Linear layout [out, in])."""
+    ln1_g: torch.Tensor
+    ln1_b: torch.Tensor
+    w_qkv: torch.Tensor
+    b_qkv: torch.Tensor
+    w_o: torch.Tensor
+    b_o: torch.Tensor
+    ln2_g: torch.Tensor
+    ln2_b: torch.Tensor
+    w_fc1: torch.Tensor
+    b_fc1: torch.Tensor
+    w_fc2: torch.Tensor
+    b_fc2: torch.Tensor
+
+    def to(self, device) -> "LayerWeights":
+        return LayerWeights(**{k: v.to(device) for k, v in self.__dict__.items()})
+
+
+def random_layer_weights(cfg: EncoderConfig, gen: torch.Generator, std: float = 0.02) -> LayerWeights:
+    """Random-init weights on the CPU: linears and biases ~ N(0, std), k bias 0, LN gamma 1 beta 0."""
+    D, Fd = cfg.d_model, cfg.ffn
+
+    def n(*shape):
+        return (torch.randn(*shape, generator=gen, dtype=torch.float32) * std).half()
+
+    b_qkv = n(3 * D)
+    b_qkv[D:2 * D] = 0  # k_proj has no bias
+    return LayerWeights(
+        ln1_g=torch.ones(D, dtype=torch.float16), ln1_b=torch.zeros(D, dtype=torch.float16),
+        w_qkv=n(3 * D, D), b_qkv=b_qkv, w_o=n(D, D), b_o=n(D),
+        ln2_g=torch.ones(D, dtype=torch.float16), ln2_b=torch.zeros(D, dtype=torch.float16),
+        w_fc1=n(Fd, D), b_fc1=n(Fd), w_fc2=n(D, Fd), b_fc2=n(D))
+
+
+@dataclass
+class _QuantLayer:
+    ln1_g: torch.Tensor
+    ln1_b: torch.Tensor
+    w_qkv: torch.Tensor
+    s_qkv: torch.Tensor
+    b_qkv: torch.Tensor
+    w_o: torch.Tensor
+    s_o: torch.Tensor
+    b_o: torch.Tensor
+    ln2_g: torch.Tensor
+    ln2_b: torch.Tensor
+    w_fc1: torch.Tensor
+    s_fc1: torch.Tensor
+    b_fc1: torch.Tensor
+    w_fc2: torch.Tensor
+    s_fc2: torch.Tensor
+    b_fc2: torch.Tensor
+
+
+@dataclass
+class GemmTiming:
+    """CUDA-event bracket around one GEMM launch (for roofline accounting)."""
+    start: torch.cuda.Event
+    end: torch.cuda.Event
+    flops: int
+    name: str = ""
+
+    def ms(self) -> float:
+        return self.start.elapsed_time(self.end)
+
+
+class FP8EncoderStack:
+    """Encoder stack on one GPU. forward() takes [B, S, D] fp16 on the device."""
+
+    def __init__(self, cfg: EncoderConfig, layers: List[LayerWeights], device,
+                 final_ln: Optional[tuple] = None) -> None:
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.layers: List[_QuantLayer] = []
+        with torch.cuda.device(self.device):
+            for lw in layers:
+                lw = lw.to(self.device)
+                wq, sq = ops.quantise(lw.w_qkv.contiguous())
+                wo, so = ops.quantise(lw.w_o.contiguous())
+                w1, s1 = ops.quantise(lw.w_fc1.contiguous())
+                w2, s2 = ops.quantise(lw.w_fc2.contiguous())
+                self.layers.append(_QuantLayer(lw.ln1_g, lw.ln1_b, wq, sq, lw.b_qkv, wo, so, lw.b_o,
+                                               lw.ln2_g, lw.ln2_b, w1, s1, lw.b_fc1, w2, s2, lw.b_fc2))
+            D = cfg.d_model
+            if final_ln is None:
+                final_ln = (torch.ones(D, dtype=torch.float16), torch.zeros(D, dtype=torch.float16))
+            self.final_g = final_ln[0].to(self.device)
+            self.final_b = final_ln[1].to(self.device)
+        self._ws_tokens = -1
+        self.gemm_timings: Optional[List[GemmTiming]] = None  # set to [] to record
+
+    # -------------------------------------------------------------- buffers
+    def _workspace(self, T: int) -> None:
+        if self._ws_tokens == T:
+            return
+        D, Fd, dev = self.cfg.d_model, self.cfg.ffn, self.device
+        e = lambda *s, dt=torch.float16: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
+        self.h_a, self.h_b, self.h2 = e(T, D), e(T, D), e(T, D)
+        self.x, self.attn = e(T, D), e(T, D)
+        self.xq, self.aq = e(T, D, dt=torch.uint8), e(T, D, dt=torch.uint8)
+        self.qkv = e(T, 3 * D)
+        self.f = e(T, Fd)
+        self.fq = e(T, Fd, dt=torch.uint8)
+        self.out = e(T, D)
+        self.amax = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.scales = torch.ones(4, dtype=torch.float32, device=dev)
+        self._ws_tokens = T
+
+    def _gemm(self, name: str, flops: int, *args, **kwargs) -> torch.Tensor:
+        if self.gemm_timings is None:
+            return ops.gemm_fp8(*args, **kwargs)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        out = ops.gemm_fp8(*args, **kwargs)
+        e.record()
+        self.gemm_timings.append(GemmTiming(s, e, flops, name))
+        return out
+
+    # -------------------------------------------------------------- compute
+    def _attention(self, B: int, S: int) -> torch.Tensor:
+        cfg = self.cfg
+        H, Dh = cfg.heads, cfg.head_dim
+        qkv = self.qkv.view(B, S, 3, H, Dh)
+        q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
+        o = F.scaled_dot_product_attention(q, k, v)  # [B, H, S, Dh]
+        o = o.transpose(1, 2)
+        if o.is_contiguous():
+            return o.reshape(B * S, cfg.d_model)
+        self.attn.view(B, S, H, Dh).copy_(o)
+        return self.attn
+
+    def _layer(self, L: _QuantLayer, h: torch.Tensor, h_next: torch.Tensor, B: int, S: int) -> None:
+        cfg = self.cfg
+        T, D, Fd = B * S, cfg.d_model, cfg.ffn
+        amax, sc = self.amax, self.scales
+        amax.zero_()
+        ops.layernorm(h, None, L.ln1_g, L.ln1_b, cfg.eps, out=self.x, out_amax=amax[0:1])
+        ops.quantise_from_amax(self.x, amax[0:1], q_out=self.xq, scale_out=sc[0:1])
+        self._gemm("qkv", 2 * T * D * 3 * D, self.xq, sc[0:1], L.w_qkv, L.s_qkv, L.b_qkv, out=self.qkv)
+        attn = self._attention(B, S)
+        ops.amax_accumulate(attn, amax[1:2])
+        ops.quantise_from_amax(attn, amax[1:2], q_out=self.aq, scale_out=sc[1:2])
+        self._gemm("out_proj", 2 * T * D * D, self.aq, sc[1:2], L.w_o, L.s_o, L.b_o, residual=h,
+                   epilogue="residual", out=self.h2)
+        ops.layernorm(self.h2, None, L.ln2_g, L.ln2_b, cfg.eps, out=self.x, out_amax=amax[2:3])
+        ops.quantise_from_amax(self.x, amax[2:3], q_out=self.xq, scale_out=sc[2:3])
+        self._gemm("fc1", 2 * T * D * Fd, self.xq, sc[2:3], L.w_fc1, L.s_fc1, L.b_fc1, epilogue="gelu",
+                   out=self.f, out_amax=amax[3:4])
+        ops.quantise_from_amax(self.f, amax[3:4], q_out=self.fq, scale_out=sc[3:4])
+        self._gemm("fc2", 2 * T * Fd * D, self.fq, sc[3:4], L.w_fc2, L.s_fc2, L.b_fc2, residual=self.h2,
+                   epilogue="residual_clamp", out=h_next)
+
+    @torch.inference_mode()
+    def forward(self, hidden: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """hidden [B, S, D] fp16 on this stack's device -> [B, S, D] fp16 (the final LayerNorm applied)."""
+        ops.require_input(hidden, "hidden")
+        ops.require_fp16(hidden, "hidden")
+        B, S, D = hidden.shape
+        if D != self.cfg.d_model:
+            raise RuntimeError(f"hidden size {D} != d_model {self.cfg.d_model}")
+        T = B * S
+        with torch.cuda.device(self.device):
+            self._workspace(T)
+            h = hidden.reshape(T, D)
+            bufs = (self.h_a, self.h_b)
+            for i, L in enumerate(self.layers):
+                nxt = bufs[i % 2]
+                self._layer(L, h, nxt, B, S)
+                h = nxt
+            o = self.out if out is None else out.view(T, D)
+            ops.layernorm(h, None, self.final_g, self.final_b, self.cfg.eps, out=o)
+        return o.view(B, S, D)
+
+    @torch.inference_mode()
+    def forward_host(self, hidden_host: torch.Tensor, out_host: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Host-to-host call: copy in (from pinned memory), run, copy out."""
+        dev_in = hidden_host.to(self.device, non_blocking=True)
+        y = self.forward(dev_in)
+        if out_host is None:
+            out_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
+        out_host.copy_(y, non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out_host

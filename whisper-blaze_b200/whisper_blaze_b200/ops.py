@@ -1,0 +1,236 @@
+"""Tensor-level wrappers over libwbk.so for torch callers.
+
+Every op runs on torch's current stream of its input's device, under a device
+guard, and never synchronises unless it must hand a value back to the host.
+Scales can stay on the device (1-element fp32 tensors), so a chain of
+quantise -> GEMM -> norm -> quantise issues no host round trip.
+"""
+from __future__ import annotations
+
+from typing import Optional, Sequence, Union
+
+import torch
+
+from . import _lib
+from ._lib import (EPI_GELU, EPI_NONE, EPI_RESIDUAL, EPI_RESIDUAL_CLAMP, FMT_E4M3, FMT_E5M2, check, lib, ptr,
+                   stream_of)
+
+Scale = Union[float, torch.Tensor]
+
+_FMT_BY_NAME = {"e4m3": FMT_E4M3, "e5m2": FMT_E5M2, FMT_E4M3: FMT_E4M3, FMT_E5M2: FMT_E5M2}
+_EPI_BY_NAME = {"none": EPI_NONE, "bias": EPI_NONE, "gelu": EPI_GELU, "residual": EPI_RESIDUAL,
+                "residual_clamp": EPI_RESIDUAL_CLAMP, EPI_NONE: EPI_NONE, EPI_GELU: EPI_GELU,
+                EPI_RESIDUAL: EPI_RESIDUAL, EPI_RESIDUAL_CLAMP: EPI_RESIDUAL_CLAMP}
+_BYTE_DTYPES = {torch.uint8, torch.int8, torch.float8_e4m3fn, torch.float8_e5m2}
+
+
+def fmt_code(fmt) -> int:
+    try:
+        return _FMT_BY_NAME[fmt]
+    except KeyError:
+        raise ValueError(f"unknown fp8 format {fmt!r}; expected 'e4m3' or 'e5m2'") from None
+
+
+def require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+
+
+def require_contig(t: torch.Tensor, name: str) -> None:
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+
+
+def require_input(t: torch.Tensor, name: str) -> None:
+    require_cuda(t, name)
+    require_contig(t, name)
+
+
+def require_fp16(t: torch.Tensor, name: str) -> None:
+    if t.dtype != torch.float16:
+        raise RuntimeError(f"{name} must be fp16")
+
+
+def require_bytes(t: torch.Tensor, name: str) -> None:
+    if t.dtype not in _BYTE_DTYPES:
+        raise RuntimeError(f"{name} must hold fp8 codes (uint8 or a float8 dtype), got {t.dtype}")
+
+
+def require_same_device(*ts: Optional[torch.Tensor]) -> None:
+    devs = {t.device for t in ts if t is not None}
+    if len(devs) > 1:
+        raise RuntimeError(f"tensors are on different devices: {sorted(map(str, devs))}")
+
+
+def new_amax_ws(device) -> torch.Tensor:
+    """A zeroed device uint32 accumulator (held as int32) for the fused amax."""
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+# ---------------------------------------------------------------- quantiser
+
+def amax_accumulate(x: torch.Tensor, amax_ws: torch.Tensor) -> torch.Tensor:
+    require_input(x, "x")
+    require_fp16(x, "x")
+    require_same_device(x, amax_ws)
+    with torch.cuda.device(x.device):
+        check(lib().wbk_amax_f16(x.data_ptr(), x.numel(), amax_ws.data_ptr(), stream_of(x)), "amax")
+    return amax_ws
+
+
+def quantise_from_amax(x: torch.Tensor, amax_ws: torch.Tensor, fmt="e4m3", q_out: Optional[torch.Tensor] = None,
+                       scale_out: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Quantise x with the scale implied by an already accumulated amax."""
+    require_input(x, "x")
+    require_fp16(x, "x")
+    f = fmt_code(fmt)
+    q = torch.empty(x.shape, dtype=torch.uint8, device=x.device) if q_out is None else q_out
+    s = torch.empty(1, dtype=torch.float32, device=x.device) if scale_out is None else scale_out
+    require_same_device(x, amax_ws, q, s)
+    with torch.cuda.device(x.device):
+        check(lib().wbk_quantise_from_amax_f16(x.data_ptr(), x.numel(), f, amax_ws.data_ptr(), q.data_ptr(),
+                                               s.data_ptr(), stream_of(x)), "quantise")
+    return q, s
+
+
+def quantise(x: torch.Tensor, fmt="e4m3", q_out: Optional[torch.Tensor] = None,
+             scale_out: Optional[torch.Tensor] = None,
+             amax_ws: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-tensor quantise; returns (codes uint8, device fp32 scale [1]). No host sync."""
+    require_input(x, "x")
+    require_fp16(x, "x")
+    f = fmt_code(fmt)
+    q = torch.empty(x.shape, dtype=torch.uint8, device=x.device) if q_out is None else q_out
+    s = torch.empty(1, dtype=torch.float32, device=x.device) if scale_out is None else scale_out
+    ws = torch.empty(1, dtype=torch.int32, device=x.device) if amax_ws is None else amax_ws
+    require_same_device(x, q, s, ws)
+    with torch.cuda.device(x.device):
+        check(lib().wbk_quantise_f16(x.data_ptr(), x.numel(), f, q.data_ptr(), s.data_ptr(), ws.data_ptr(),
+                                     stream_of(x)), "quantise")
+    return q, s
+
+
+def dequantise(q: torch.Tensor, scale: float, shape: Sequence[int], fmt="e4m3") -> torch.Tensor:
+    require_input(q, "fp8")
+    require_bytes(q, "fp8")
+    f = fmt_code(fmt)
+    shape = [int(d) for d in shape]
+    out = torch.empty(shape, dtype=torch.float16, device=q.device)
+    if out.numel() != q.numel():
+        raise RuntimeError(f"shape {shape} holds {out.numel()} elements but fp8 has {q.numel()}")
+    with torch.cuda.device(q.device):
+        check(lib().wbk_dequantise_f16(q.data_ptr(), q.numel(), f, float(scale), out.data_ptr(), stream_of(q)),
+              "dequantise")
+    return out
+
+
+# -------------------------------------------------------------------- norms
+
+def layernorm(x: torch.Tensor, residual: Optional[torch.Tensor], gamma: torch.Tensor, beta: torch.Tensor,
+              eps: float = 1e-5, want_sum: bool = False, out: Optional[torch.Tensor] = None,
+              sum_out: Optional[torch.Tensor] = None,
+              out_amax: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, Optional[torch.Tensor]]:
+    require_input(x, "x")
+    require_input(gamma, "gamma")
+    require_input(beta, "beta")
+    require_fp16(x, "x")
+    require_fp16(gamma, "gamma")
+    require_fp16(beta, "beta")
+    if residual is not None:
+        require_input(residual, "residual")
+        require_fp16(residual, "residual")
+        if residual.shape != x.shape:
+            raise RuntimeError("residual must have the same shape as x")
+    if x.dim() == 0:
+        raise RuntimeError("x must have at least one dimension")
+    D = x.shape[-1]
+    if gamma.numel() != D or beta.numel() != D:
+        raise RuntimeError(f"gamma and beta must have {D} elements")
+    rows = x.numel() // D if D else 0
+    o = torch.empty_like(x) if out is None else out
+    s = (torch.empty_like(x) if sum_out is None else sum_out) if want_sum else None
+    require_same_device(x, residual, gamma, beta, o, s, out_amax)
+    with torch.cuda.device(x.device):
+        check(lib().wbk_layernorm_f16(x.data_ptr(), ptr(residual), gamma.data_ptr(), beta.data_ptr(), o.data_ptr(),
+                                      ptr(s), rows, D, float(eps), ptr(out_amax), stream_of(x)), "layernorm_fused")
+    return o, s
+
+
+def rmsnorm(x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    require_input(x, "x")
+    require_input(residual, "residual")
+    require_input(gamma, "gamma")
+    require_fp16(x, "x")
+    require_fp16(residual, "residual")
+    require_fp16(gamma, "gamma")
+    if residual.shape != x.shape:
+        raise RuntimeError("residual must have the same shape as x")
+    D = x.shape[-1]
+    if gamma.numel() != D:
+        raise RuntimeError(f"gamma must have {D} elements")
+    out = torch.empty_like(x)
+    require_same_device(x, residual, gamma)
+    with torch.cuda.device(x.device):
+        check(lib().wbk_rmsnorm_f16(x.data_ptr(), residual.data_ptr(), gamma.data_ptr(), out.data_ptr(),
+                                    x.numel() // D, D, float(eps), stream_of(x)), "rmsnorm_fused")
+    return out
+
+
+# --------------------------------------------------------------------- GEMM
+
+def _scale_arg(scale: Scale, name: str, device) -> tuple[float, Optional[int]]:
+    if isinstance(scale, torch.Tensor):
+        if scale.numel() != 1 or scale.dtype != torch.float32 or not scale.is_cuda:
+            raise RuntimeError(f"{name} must be a Python float or a 1-element fp32 CUDA tensor")
+        if scale.device != device:
+            raise RuntimeError(f"{name} is on {scale.device}, expected {device}")
+        return 1.0, scale.data_ptr()
+    return float(scale), None
+
+
+def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
+             bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None, epilogue="none",
+             a_format="e4m3", w_format="e4m3", out: Optional[torch.Tensor] = None,
+             out_amax: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[..., N] = epilogue(dq(a)[..., K] @ dq(w)[N, K]^T + bias); fp16 output.
+
+    a: fp8 codes [..., K]; w: fp8 codes [N, K] (nn.Linear layout); scales as
+    Python floats or 1-element fp32 CUDA tensors; epilogue one of
+    'none' | 'gelu' | 'residual' | 'residual_clamp'.
+    """
+    require_input(a, "a_fp8")
+    require_input(w, "w_fp8")
+    require_bytes(a, "a_fp8")
+    require_bytes(w, "w_fp8")
+    if w.dim() != 2:
+        raise RuntimeError("w_fp8 must be 2-D [N, K]")
+    N, K = w.shape
+    if a.dim() < 1 or a.shape[-1] != K:
+        raise RuntimeError(f"a_fp8 last dimension {a.shape[-1] if a.dim() else None} != K={K}")
+    M = a.numel() // K if K else 0
+    epi = _EPI_BY_NAME.get(epilogue)
+    if epi is None:
+        raise ValueError(f"unknown epilogue {epilogue!r}")
+    out_shape = tuple(a.shape[:-1]) + (N,)
+    if bias is not None:
+        require_input(bias, "bias")
+        require_fp16(bias, "bias")
+        if bias.numel() != N:
+            raise RuntimeError(f"bias must have {N} elements")
+    if residual is not None:
+        require_input(residual, "residual")
+        require_fp16(residual, "residual")
+        if residual.numel() != M * N:
+            raise RuntimeError(f"residual must have shape {out_shape}")
+    if epi in (EPI_RESIDUAL, EPI_RESIDUAL_CLAMP) and residual is None:
+        raise RuntimeError("residual epilogue requires a residual tensor")
+    alpha_a, pa = _scale_arg(a_scale, "a_scale", a.device)
+    alpha_w, pw = _scale_arg(w_scale, "w_scale", a.device)
+    alpha = float(torch.tensor(alpha_a, dtype=torch.float32) * torch.tensor(alpha_w, dtype=torch.float32))
+    o = torch.empty(out_shape, dtype=torch.float16, device=a.device) if out is None else out
+    require_same_device(a, w, bias, residual, o, out_amax)
+    with torch.cuda.device(a.device):
+        check(lib().wbk_gemm_fp8(a.data_ptr(), w.data_ptr(), M, N, K, fmt_code(a_format), fmt_code(w_format), alpha,
+                                 pa, pw, ptr(bias), ptr(residual), o.data_ptr(), epi, ptr(out_amax), stream_of(a)),
+              "gemm_fp8")
+    return o

@@ -1,0 +1,126 @@
+"""`whisper_blaze_kernels` — drop-in op surface of whisper-blaze, on B200 kernels.
+
+Same module name, function names, argument names, defaults, return types and
+error type (RuntimeError for argument checks) as the reference's pybind
+module (csrc/ops/bindings.cpp:181-240), so `import whisper_blaze_kernels` in
+whisper_blaze/model.py binds to these without change. Every op launches a
+hand-written sm_100a kernel from libwbk.so on torch's current stream.
+
+Differences that only remove hazards of the reference:
+  * tails: inputs whose element count is not a multiple of 8 are quantised
+    completely (the reference leaves the tail unwritten, fp8_quantize.cu:229);
+  * dequantise checks that `shape` holds as many elements as `fp8` (the
+    reference writes past a smaller output);
+  * a last dimension that is not a multiple of 8 is rejected by the norms
+    (the reference reads it out of bounds; BlazeLayerNorm.supports already
+    routes such shapes to torch).
+
+Added (not in the reference): `gemm_fp8_e4m3` / `gemm_fp8`, the FP8 scaled GEMM
+the precision.py linear layers need, and `quantise_e4m3_dev`, which keeps the
+scale on the device instead of returning a Python float.
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Sequence, Tuple
+
+import torch
+
+from whisper_blaze_b200 import ops as _ops
+from whisper_blaze_b200._lib import lib as _lib
+
+_lib()  # fail at import time, loudly, if libwbk.so is missing
+
+
+def _quantise_host_scale(fp16: torch.Tensor, fmt: str) -> Tuple[torch.Tensor, float]:
+    _ops.require_input(fp16, "fp16")
+    _ops.require_fp16(fp16, "fp16")
+    q, s = _ops.quantise(fp16, fmt)
+    return q, float(s.item())  # host float, as the reference returns (one device sync)
+
+
+def quantise_e4m3(fp16: torch.Tensor) -> Tuple[torch.Tensor, float]:
+    """Quantise FP16 tensor to FP8 E4M3. Returns (fp8_tensor, scale)."""
+    return _quantise_host_scale(fp16, "e4m3")
+
+
+def quantise_e5m2(fp16: torch.Tensor) -> Tuple[torch.Tensor, float]:
+    """Quantise FP16 tensor to FP8 E5M2. Returns (fp8_tensor, scale)."""
+    return _quantise_host_scale(fp16, "e5m2")
+
+
+def quantise_e4m3_dev(fp16: torch.Tensor, fmt: str = "e4m3") -> Tuple[torch.Tensor, torch.Tensor]:
+    """Quantise without a host sync: returns (fp8_tensor, scale as a 1-element fp32 CUDA tensor)."""
+    _ops.require_input(fp16, "fp16")
+    _ops.require_fp16(fp16, "fp16")
+    return _ops.quantise(fp16, fmt)
+
+
+def dequantise_e4m3(fp8: torch.Tensor, scale: float, shape: Sequence[int]) -> torch.Tensor:
+    """Dequantise FP8 E4M3 tensor to FP16."""
+    return _ops.dequantise(fp8, scale, shape, "e4m3")
+
+
+def dequantise_e5m2(fp8: torch.Tensor, scale: float, shape: Sequence[int]) -> torch.Tensor:
+    """Dequantise FP8 E5M2 tensor to FP16."""
+    return _ops.dequantise(fp8, scale, shape, "e5m2")
+
+
+def layernorm_fused(x: torch.Tensor, residual: Optional[torch.Tensor] = None, gamma: torch.Tensor = None,
+                    beta: torch.Tensor = None, epsilon: float = 1e-5) -> torch.Tensor:
+    """Fused residual-add + LayerNorm -> FP16. residual=None gives a plain LayerNorm."""
+    if gamma is None or beta is None:
+        raise TypeError("layernorm_fused() missing required argument 'gamma' or 'beta'")
+    return _ops.layernorm(x, residual, gamma, beta, epsilon)[0]
+
+
+def layernorm_fused_residual(x: torch.Tensor, residual: Optional[torch.Tensor] = None, gamma: torch.Tensor = None,
+                             beta: torch.Tensor = None, epsilon: float = 1e-5) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Fused residual-add + LayerNorm -> (normalised, x+residual)."""
+    if gamma is None or beta is None:
+        raise TypeError("layernorm_fused_residual() missing required argument 'gamma' or 'beta'")
+    out, s = _ops.layernorm(x, residual, gamma, beta, epsilon, want_sum=True)
+    return out, s
+
+
+def rmsnorm_fused(x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor, epsilon: float = 1e-5) -> torch.Tensor:
+    """Fused residual-add + RMSNorm -> FP16."""
+    return _ops.rmsnorm(x, residual, gamma, epsilon)
+
+
+def gemm_fp8_e4m3(a_fp8: torch.Tensor, a_scale, w_fp8: torch.Tensor, w_scale, bias: Optional[torch.Tensor] = None,
+                  residual: Optional[torch.Tensor] = None, epilogue: str = "none",
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """FP8 E4M3 scaled GEMM: fp16(epilogue(dq(a)[M,K] @ dq(w)[N,K]^T + bias)).
+
+    Scales are Python floats or 1-element fp32 CUDA tensors. epilogue is
+    'none', 'gelu' (exact erf), 'residual' or 'residual_clamp'.
+    """
+    return _ops.gemm_fp8(a_fp8, a_scale, w_fp8, w_scale, bias, residual, epilogue, "e4m3", "e4m3", out)
+
+
+def gemm_fp8(a_fp8: torch.Tensor, a_scale, w_fp8: torch.Tensor, w_scale, bias: Optional[torch.Tensor] = None,
+             residual: Optional[torch.Tensor] = None, epilogue: str = "none", a_format: str = "e4m3",
+             w_format: str = "e4m3", out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """FP8 scaled GEMM with per-operand formats ('e4m3' or 'e5m2')."""
+    return _ops.gemm_fp8(a_fp8, a_scale, w_fp8, w_scale, bias, residual, epilogue, a_format, w_format, out)
+
+
+def _out_of_scope(name: str):
+    def fn(*args, **kwargs):
+        raise NotImplementedError(
+            f"whisper_blaze_kernels.{name} is outside the FP8 quantised-matmul path rebuilt for B200 "
+            f"(attention runs in torch SDPA, mel features in the HF processor)")
+    fn.__name__ = name
+    return fn
+
+
+mel_spectrogram = _out_of_scope("mel_spectrogram")
+encoder_self_attn = _out_of_scope("encoder_self_attn")
+decoder_cross_attn = _out_of_scope("decoder_cross_attn")
+decoder_self_attn = _out_of_scope("decoder_self_attn")
+
+__all__: List[str] = [
+    "quantise_e4m3", "quantise_e5m2", "quantise_e4m3_dev", "dequantise_e4m3", "dequantise_e5m2",
+    "layernorm_fused", "layernorm_fused_residual", "rmsnorm_fused", "gemm_fp8_e4m3", "gemm_fp8",
+    "mel_spectrogram", "encoder_self_attn", "decoder_cross_attn", "decoder_self_attn",
+]
