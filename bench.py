@@ -1,0 +1,439 @@
+"""Benchmark of the B200 FP8 quantised-matmul path (whisper-blaze north star).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload stack|layer|fc1|decoder|crossattn]
+
+Default workload (config 5 of the north star): a 32-layer Whisper-large-v3
+encoder stack (d_model 1280, 20 heads, FFN 5120, pre-LN, every linear FP8
+E4M3 per-tensor scaled, fp16 torch-SDPA attention), random-init weights,
+synthetic post-conv hidden states [64 chunks, 1500, 1280] fp16 ~ N(0,1).
+The 64 chunks are split by batch over N GPUs (one process per GPU under
+torchrun, NCCL), outputs gathered with one all_gather_into_tensor. A step is
+one pass of the whole stack over the whole batch plus the gather; metric
+chunks/s = 64 / max-over-ranks step time (strong scaling: total work fixed).
+
+Prints ONE JSON line on rank 0. `value` has the inputs resident in HBM;
+`e2e` is the same metric through the public host API (pinned host input ->
+device, stack, gather, device -> host output on rank 0), copies timed.
+`roofline` is for the dominant kernel (the tcgen05 FP8 GEMM): achieved
+TFLOP/s = algorithmic FLOPs of the GEMM launches in the timed steps / their
+CUDA-event time. `cpu_baseline` (rank 0, N = 1) and `--impl reference` time
+the reference's CPU path (torch-CPU fp32 dequantise + matmul, oracle/encoder.py)
+on one chunk on all host cores.
+
+Secondary workloads print their own line with their
+own metric: fc1 (config 1), layer (config 2), decoder (config 3), crossattn
+(config 4).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [REPO, os.path.join(REPO, "whisper-blaze_b200")]
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+TOTAL_CHUNKS = 64
+NOMINAL_FP8_TFLOPS = 4500.0
+
+
+# ----------------------------------------------------------------- helpers
+
+def measured_peaks() -> dict:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"],
+                "bf16_tflops_sustained": p.get("bf16_tflops_sustained", p["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def fp8_peak(sustained: bool) -> tuple[float, str]:
+    p = measured_peaks()
+    key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
+    return 2.0 * p[key], (f"2 x {key} of {p['source']} MEASURED_PEAKS.json "
+                          f"(dense fp8 tensor rate is 2x dense bf16 on B200)")
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"wbk_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                    rows.append(parts)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+
+
+def setup_dist():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(v: float, world: int, device) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(v: float, world: int, device) -> float:
+    if world == 1:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        dist.barrier()
+
+
+def roofline_traffic(kernel_key: str):
+    """dram bytes per launch from a committed ncu capture summary, if any."""
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            return json.load(f).get(kernel_key)
+    return None
+
+
+# ------------------------------------------------------------ CPU reference
+
+def cpu_reference_chunk(cfg, layers_fp16, budget_s: float) -> dict:
+    from oracle import encoder as ref_encoder
+    qlayers = [ref_encoder.quantise_layer(lw) for lw in layers_fp16]
+    return ref_encoder.time_cpu_chunk(qlayers, cfg.seq_len, cfg.d_model, cfg.heads, cfg.layers, budget_s=budget_s)
+
+
+def cpu_layers(cfg, n_distinct: int = 2):
+    """Distinct random layers for the CPU path (cycled through the 32 layers: the
+    arithmetic per layer does not depend on which random weights it holds)."""
+    from whisper_blaze_b200.encoder import random_layer_weights
+    g = torch.Generator().manual_seed(0)
+    return [random_layer_weights(cfg, g) for _ in range(n_distinct)]
+
+
+def run_reference_arm(args, world, rank):
+    if rank != 0:
+        return
+    from whisper_blaze_b200.encoder import EncoderConfig
+    cfg = EncoderConfig(layers=args.layers)
+    layers = cpu_layers(cfg)
+    budget = max(2.0, args.ref_step_budget)
+    samples = []
+    info = None
+    for i in range(args.warmup + args.steps):
+        info = cpu_reference_chunk(cfg, layers, budget)
+        if i >= args.warmup:
+            samples.append(info["chunk_seconds"])
+    chunk_s = statistics.median(samples)
+    v = 1.0 / chunk_s
+    line = {
+        "impl": "reference", "metric": "encoder chunks/s (32-layer FP8 Whisper-large-v3 encoder stack)",
+        "value": v, "unit": "chunks/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": chunk_s * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "fp32 (fp8 codes dequantised)", "data": "synthetic",
+        "config": {"workload": "encoder_stack (config 5)", "global_batch": TOTAL_CHUNKS, "seq_len": cfg.seq_len,
+                   "d_model": cfg.d_model, "layers": cfg.layers, "parallelism": "host cores"},
+        "cpu_baseline": {"value": v, "unit": "chunks/s", "cores": info["threads"], "kind": "port",
+                         "sample": f"1 chunk (1500 frames), {info['layers_run']} of {cfg.layers} layers per step "
+                                   f"timed, per-layer mean extrapolated to {cfg.layers}; torch-CPU fp32 "
+                                   f"dequantise+matmul (oracle/encoder.py)"},
+        "e2e": {"value": v, "unit": "chunks/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- stack (ours)
+
+def run_stack(args, world, rank, local):
+    from whisper_blaze_b200 import ops
+    from whisper_blaze_b200.encoder import EncoderConfig, FP8EncoderStack, LayerWeights
+    from whisper_blaze_b200.sharding import gather_batch, shard_bounds
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = EncoderConfig(layers=args.layers)
+    D, Fd = cfg.d_model, cfg.ffn
+
+    # random-init weights, generated on the device from a seeded generator (identical on every rank)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234)
+
+    def n(*shape):
+        return (torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32) * 0.02).half()
+
+    layers = []
+    for _ in range(cfg.layers):
+        b_qkv = n(3 * D)
+        b_qkv[D:2 * D] = 0
+        layers.append(LayerWeights(
+            ln1_g=torch.ones(D, dtype=torch.float16, device=dev), ln1_b=torch.zeros(D, dtype=torch.float16, device=dev),
+            w_qkv=n(3 * D, D), b_qkv=b_qkv, w_o=n(D, D), b_o=n(D),
+            ln2_g=torch.ones(D, dtype=torch.float16, device=dev), ln2_b=torch.zeros(D, dtype=torch.float16, device=dev),
+            w_fc1=n(Fd, D), b_fc1=n(Fd), w_fc2=n(D, Fd), b_fc2=n(D)))
+    stack = FP8EncoderStack(cfg, layers, dev)
+    del layers
+
+    start, stop = shard_bounds(TOTAL_CHUNKS, world, rank)
+    local_b = stop - start
+    gx = torch.Generator(device=dev)
+    gx.manual_seed(99 + rank)
+    x = torch.randn(local_b, cfg.seq_len, D, generator=gx, device=dev, dtype=torch.float32).half()
+
+    def step():
+        y = stack.forward(x)
+        if world > 1:
+            return gather_batch(y, TOTAL_CHUNKS)
+        return y
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+
+    stream = torch.cuda.current_stream(dev)
+    launches0 = ops.LAUNCHES[0]
+    stack.gemm_timings = []
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    launches = ops.LAUNCHES[0] - launches0
+    ms_local = t0.elapsed_time(t1) / args.steps
+    ms = max_over_ranks(ms_local, world, dev)
+    gemm_ms = sum(t.ms() for t in stack.gemm_timings)
+    gemm_flops = sum(t.flops for t in stack.gemm_timings)
+    n_gemm = len(stack.gemm_timings)
+    stack.gemm_timings = None
+    clock_info = clocks.summary()
+
+    # e2e through the public host API: pinned host shard in, full output on rank 0's host out
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty((TOTAL_CHUNKS, cfg.seq_len, D), dtype=torch.float16, pin_memory=True) if rank == 0 else None
+    e2e_steps = max(1, min(args.steps, 5))
+
+    def e2e_step():
+        dev_in = x_host.to(dev, non_blocking=True)
+        y = stack.forward(dev_in)
+        full = gather_batch(y, TOTAL_CHUNKS) if world > 1 else y
+        if rank == 0:
+            out_host.copy_(full, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world, dev)
+    h2d = sum_over_ranks(float(x_host.numel() * 2), world, dev)
+    d2h = TOTAL_CHUNKS * cfg.seq_len * D * 2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from whisper_blaze_b200.encoder import EncoderConfig as _C
+        ccfg = _C(layers=args.layers)
+        info = cpu_reference_chunk(ccfg, cpu_layers(ccfg), args.cpu_budget)
+        cpu = {"value": info["chunks_per_s"], "unit": "chunks/s", "cores": info["threads"], "kind": "port",
+               "sample": f"1 chunk (1500 frames) x {info['layers_run']} of {ccfg.layers} layers timed "
+                         f"({info['chunk_seconds'] / ccfg.layers * info['layers_run']:.1f} s), per-layer mean "
+                         f"extrapolated to {ccfg.layers} layers; torch-CPU fp32 dequantise+matmul "
+                         f"(oracle/encoder.py), fp32 SDPA"}
+
+    if rank == 0:
+        peak, peak_src = fp8_peak(sustained=True)
+        achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+        value = TOTAL_CHUNKS / (ms * 1e-3)
+        line = {
+            "metric": "encoder chunks/s (32-layer FP8 Whisper-large-v3 encoder stack)",
+            "value": value, "unit": "chunks/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp8 e4m3 (fp32 accumulate, fp16 activations, fp16 SDPA)", "data": "synthetic",
+            "config": {"workload": "encoder_stack (config 5)", "global_batch": TOTAL_CHUNKS,
+                       "seq_len": cfg.seq_len, "d_model": D, "heads": cfg.heads, "ffn": Fd, "layers": cfg.layers,
+                       "parallelism": f"batch-sharded dp{world}, NCCL all_gather of outputs",
+                       "l2": "inputs and every activation > 126 MB L2 (no flush needed)"},
+            "e2e": {"value": TOTAL_CHUNKS / (e2e_ms * 1e-3), "unit": "chunks/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
+            "roofline": {"bound": "tensor", "kernel": "wbk fp8_gemm_kernel (tcgen05 kind::f8f6f4)",
+                         "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                         "frac": (achieved / peak) if achieved else None, "peak_source": peak_src,
+                         "frac_of_nominal_fp8_4500": (achieved / NOMINAL_FP8_TFLOPS) if achieved else None,
+                         "gemm_launches_timed": n_gemm, "gemm_ms_per_step": gemm_ms / args.steps,
+                         "gemm_share_of_step": (gemm_ms / args.steps) / ms_local,
+                         "traffic": roofline_traffic("fp8_gemm_stack")},
+            "gpu_launches": launches,
+            "clocks": clock_info,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------- secondary configs
+
+def _timeit(fn, steps, warmup):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+def run_gemm_configs(args, world, rank, local):
+    """Configs 1-4: per-GEMM TFLOP/s (or GB/s for the memory-bound decoder step)."""
+    from whisper_blaze_b200 import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    wl = args.workload
+    if wl == "fc1":
+        shapes = [("fc1", 1500, 5120, 1280, "none")]
+    elif wl == "layer":
+        shapes = [("qkv", 24000, 3840, 1280, "none"), ("out_proj", 24000, 1280, 1280, "residual"),
+                  ("fc1", 24000, 5120, 1280, "gelu"), ("fc2", 24000, 1280, 5120, "residual")]
+    elif wl == "decoder":
+        shapes = [(f"dec_n{n}", 64, n, 1280, "none") for n in (1280, 3840, 5120, 51866)]
+    else:
+        shapes = [("cross_kv", 48000, 2560, 1280, "none")]
+    peak_t, src_t = fp8_peak(sustained=False)
+    results = {}
+    tot_flops = tot_ms = 0.0
+    for name, M, N, K, epi in shapes:
+        x = torch.randn(M, K, generator=g, device=dev).half()
+        w = (torch.randn(N, K, generator=g, device=dev) * 0.02).half()
+        b = (torch.randn(N, generator=g, device=dev) * 0.02).half()
+        res = torch.randn(M, N, generator=g, device=dev).half() if epi == "residual" else None
+        xq, sx = ops.quantise(x)
+        wq, sw = ops.quantise(w)
+        out = torch.empty(M, N, dtype=torch.float16, device=dev)
+        ms = _timeit(lambda: ops.gemm_fp8(xq, sx, wq, sw, b, res, epi, out=out), args.steps, args.warmup)
+        qms = _timeit(lambda: ops.quantise(x), args.steps, args.warmup)
+        flops = 2.0 * M * N * K
+        nbytes = M * K * 2 + N * K + 2 * N + 2 * M * N + (2 * M * N if res is not None else 0)
+        results[name] = {"M": M, "N": N, "K": K, "epilogue": epi, "gemm_ms": ms,
+                         "tflops": flops / ms / 1e9, "gbs_with_fp16_A": nbytes / ms / 1e6,
+                         "quantise_A_ms": qms, "quantise_A_gbs": 3 * M * K / qms / 1e6}
+        tot_flops += flops
+        tot_ms += ms
+    if wl == "decoder":
+        hbm = measured_peaks()["hbm_gbs"]
+        # bytes = 2MK (A fp16, quantised in-call) + NK (W fp8) + 2N (bias) + 2MN (out)
+        tot_bytes = sum(2 * 64 * 1280 + r["N"] * 1280 + 2 * r["N"] + 2 * 64 * r["N"] for r in results.values())
+        tot_t = sum(r["gemm_ms"] + r["quantise_A_ms"] for r in results.values())
+        value = tot_bytes / tot_t / 1e6
+        line = {"metric": "decoder-step FP8 GEMM HBM GB/s (quantise A + GEMM)", "value": value, "unit": "GB/s",
+                "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s", "frac": value / hbm}}
+    else:
+        value = tot_flops / tot_ms / 1e9
+        line = {"metric": "FP8 GEMM TFLOP/s", "value": value, "unit": "TFLOP/s",
+                "roofline": {"bound": "tensor", "achieved": value, "peak": peak_t, "unit": "TFLOP/s",
+                             "frac": value / peak_t, "peak_source": src_t,
+                             "frac_of_nominal_fp8_4500": value / NOMINAL_FP8_TFLOPS}}
+    line.update({"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                 "dtype": "fp8 e4m3", "data": "synthetic", "config": {"workload": wl, "shapes": results}})
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["stack", "layer", "fc1", "decoder", "crossattn"], default="stack")
+    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--cpu-budget", type=float, default=20.0)
+    ap.add_argument("--ref-step-budget", type=float, default=8.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = setup_dist()
+    try:
+        if args.impl == "reference":
+            run_reference_arm(args, world, rank)
+        elif args.workload == "stack":
+            run_stack(args, world, rank, local)
+        else:
+            run_gemm_configs(args, world, rank, local)
+    finally:
+        if world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

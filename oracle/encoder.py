@@ -29,8 +29,8 @@ from . import fp8, gemm, norm
 
 
 def _q(t16: torch.Tensor):
-    q, s = fp8.quantise(t16.numpy(), fp8.E4M3)
-    return torch.from_numpy(q), float(s)
+    q, s = fp8.quantise_torch(t16, fp8.E4M3)
+    return q, float(s)
 
 
 def quantise_layer(lw) -> dict:

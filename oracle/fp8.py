@@ -127,6 +127,26 @@ def quantise(x: np.ndarray, fmt: int = E4M3) -> tuple[np.ndarray, np.float32]:
     return quantise_with_scale(x, scale, fmt), scale
 
 
+def quantise_torch(x, fmt: int = E4M3):
+    """Same rule as quantise(), vectorised on torch-CPU (multi-threaded) for the
+    timed CPU path: amax ignoring NaN, IEEE scale, fp32 multiply, NaN -> -max,
+    clamp, torch's round-to-nearest-even fp8 cast (bit-identical to
+    encode_rne_satfinite on clamped values, see tests/test_oracle_fp8.py).
+    Returns (uint8 codes tensor, float32 scale)."""
+    import torch
+    xf = x.float()
+    a = xf.abs()
+    a = torch.where(torch.isnan(a), torch.zeros_like(a), a)
+    amax = np.float32(a.max().item()) if a.numel() else np.float32(0.0)
+    scale = scale_from_amax(amax, fmt)
+    inv = float(inv_scale(scale))
+    mx = float(FMT_MAX[fmt])
+    f = xf * torch.tensor(inv, dtype=torch.float32)
+    c = torch.where(torch.isnan(f), torch.full_like(f, -mx), f.clamp(-mx, mx))
+    dt = torch.float8_e4m3fn if fmt == E4M3 else torch.float8_e5m2
+    return c.to(dt).view(torch.uint8), scale
+
+
 def dequantise(q: np.ndarray, scale: float, fmt: int = E4M3) -> np.ndarray:
     """Reference dequantise: fp16(float(q) * scale)."""
     with np.errstate(over="ignore", invalid="ignore"):

@@ -16,11 +16,16 @@
 //   * warp 1: TMEM owner + single-thread tcgen05.mma issuer
 //     (kind::f8f6f4, M=128 N=256 K=32, fp32 accumulate), committing each stage
 //     back to the producer and each finished tile to the epilogue;
-//   * warps 2-5: epilogue. Two 256-column fp32 accumulators in TMEM (all 512
-//     columns) so the epilogue of tile i overlaps the MMAs of tile i+1; each
-//     warp drains its 32 TMEM lanes with tcgen05.ld, applies descale, bias,
-//     exact-erf GELU or residual add (+ optional fp16 clamp), rounds to fp16,
-//     stores, and tracks max|out| for a fused per-tensor amax.
+//   * warps 2-9: epilogue. Two 256-column fp32 accumulators in TMEM (all 512
+//     columns) so the epilogue of tile i overlaps the MMAs of tile i+1. Warp w
+//     may only touch TMEM lanes 32*(w%4)..+31, so two warps share each lane
+//     quarter and split the 256 columns in halves. Each drains 32-column
+//     chunks with double-buffered tcgen05.ld, applies descale, bias, exact-erf
+//     GELU or residual add (+ fp16 clamp), rounds to fp16, tracks max|out|,
+//     and writes the chunk through a 64B-swizzled shared-memory staging
+//     buffer with a TMA bulk-tensor store (coalesced, asynchronous, clipped at
+//     the M/N edges by the hardware). Outputs whose row pitch is not a multiple
+//     of 16 bytes (N % 8 != 0) are stored directly from registers instead.
 //
 // Every mbarrier wait is bounded (wall-clock limit via %globaltimer): a wait
 // that runs out records WBK_ERR_DEVICE_TIMEOUT in a device word, raises a
@@ -50,7 +55,11 @@ constexpr int A_STAGE_BYTES = BM * BK;  // 16 KB
 constexpr int B_STAGE_BYTES = BN * BK;  // 32 KB
 constexpr int NUM_ACC = 2;
 constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;
+constexpr int THREADS = 64 + EPI_WARPS * 32;  // 320
+constexpr int EPI_COLS = BN / 2;              // columns per epilogue warp
+constexpr int CHUNK = 32;                     // columns per tcgen05.ld / per TMA store box
+constexpr int STAGE_OUT_BYTES = 32 * CHUNK * 2;  // 32 rows x 32 fp16 = 2 KB
 
 enum : uint32_t {
   SITE_PRODUCER_EMPTY = 1,
@@ -64,6 +73,7 @@ enum : uint32_t {
 struct SharedStorage {
   uint8_t a[STAGES][A_STAGE_BYTES];  // 1024-byte aligned (swizzle atom)
   uint8_t b[STAGES][B_STAGE_BYTES];
+  uint8_t out[EPI_WARPS][2][STAGE_OUT_BYTES];  // per-warp double-buffered store staging
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t acc_full[NUM_ACC];
@@ -74,6 +84,7 @@ struct SharedStorage {
 };
 constexpr size_t SMEM_BYTES = sizeof(SharedStorage) + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+static_assert(EPI_COLS / CHUNK == 4, "the epilogue drain below is unrolled for 4 chunks per warp");
 
 struct Params {
   int M, N, K;
@@ -85,6 +96,7 @@ struct Params {
   const __half* residual;
   __half* out;
   uint32_t* out_amax;
+  int out_pairs;  // direct-store path: rows 4-byte aligned, store fp16 pairs
   uint32_t idesc;
   uint64_t timeout_ns;
 };
@@ -162,6 +174,23 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// Shared -> global tensor store of one box; completion tracked by bulk groups.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed store groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Make this thread's generic-proxy shared-memory writes visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -209,7 +238,20 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t* r) 
         "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
-__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Wait for this thread's outstanding tcgen05.ld. The registers of the load
+// being waited on are tied to the wait ("+r"), so the compiler cannot move any
+// use of them above it.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t* r) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
 
 // Shared-memory matrix descriptor for a K-major operand tile written by TMA
 // with 128-byte swizzle: rows of 128 bytes, 8-row (1024-byte) swizzle atoms
@@ -235,11 +277,23 @@ __device__ __forceinline__ float epi_apply(float v) {
   return v;
 }
 
-// Processes one 32-column chunk of one row (this thread's row) and stores it.
+__device__ __forceinline__ void add_halves8(float* v, const uint4& raw) {
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int t = 0; t < 4; ++t) {
+    const float2 f = __half22float2(h[t]);
+    v[2 * t] += f.x;
+    v[2 * t + 1] += f.y;
+  }
+}
+
+// fp32 accumulators of one 32-column chunk of this thread's row -> epilogue
+// values in fp32 (descale, bias, activation, residual, clamp). Columns >= N
+// and rows >= M are never read from global memory.
 template <int kEpi, bool kVec>
-__device__ __forceinline__ uint32_t epi_chunk(const Params& p, const uint32_t* acc, int row, int col0, float descale) {
+__device__ __forceinline__ void epi_values(const Params& p, const uint32_t* acc, int row, int col0, float descale,
+                                           float* v) {
   const int N = p.N;
-  float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]) * descale;
   const bool full = kVec && (col0 + 32 <= N);
@@ -247,16 +301,7 @@ __device__ __forceinline__ uint32_t epi_chunk(const Params& p, const uint32_t* a
     if (full) {
       const uint4* bv = reinterpret_cast<const uint4*>(p.bias + col0);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 b = __ldg(bv + q);
-        const __half2* h = reinterpret_cast<const __half2*>(&b);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float2 f = __half22float2(h[t]);
-          v[q * 8 + 2 * t] += f.x;
-          v[q * 8 + 2 * t + 1] += f.y;
-        }
-      }
+      for (int q = 0; q < 4; ++q) add_halves8(v + 8 * q, __ldg(bv + q));
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
@@ -266,65 +311,46 @@ __device__ __forceinline__ uint32_t epi_chunk(const Params& p, const uint32_t* a
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = epi_apply<kEpi>(v[j]);
   if (kEpi == WBK_EPI_RESIDUAL || kEpi == WBK_EPI_RESIDUAL_CLAMP) {
-    const __half* rrow = p.residual + static_cast<int64_t>(row) * N;
-    if (full) {
-      const uint4* rv = reinterpret_cast<const uint4*>(rrow + col0);
+    if (row < p.M) {
+      const __half* rrow = p.residual + static_cast<int64_t>(row) * N;
+      if (full) {
+        const uint4* rv = reinterpret_cast<const uint4*>(rrow + col0);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 r = __ldg(rv + q);
-        const __half2* h = reinterpret_cast<const __half2*>(&r);
+        for (int q = 0; q < 4; ++q) add_halves8(v + 8 * q, __ldg(rv + q));
+      } else {
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const float2 f = __half22float2(h[t]);
-          v[q * 8 + 2 * t] += f.x;
-          v[q * 8 + 2 * t + 1] += f.y;
-        }
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < N) v[j] += __half2float(rrow[col0 + j]);
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) v[j] += __half2float(rrow[col0 + j]);
     }
     if (kEpi == WBK_EPI_RESIDUAL_CLAMP) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = fminf(fmaxf(v[j], -64504.0f), 64504.0f);
     }
   }
-  __half* orow = p.out + static_cast<int64_t>(row) * N;
+}
+
+// Rounds v to fp16 into 16 packed words; returns max|fp16| over valid columns.
+__device__ __forceinline__ uint32_t pack_fp16(const float* v, uint32_t* w, int valid_cols) {
   uint32_t m = 0;
-  if (full) {
-    uint4* ov = reinterpret_cast<uint4*>(orow + col0);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 o;
-      uint32_t* w = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const __half2 h = __halves2half2(__float2half_rn(v[q * 8 + 2 * t]), __float2half_rn(v[q * 8 + 2 * t + 1]));
-        w[t] = *reinterpret_cast<const uint32_t*>(&h);
-        m = __vmaxu2(m, abs2_nonan(w[t]));
-      }
-      ov[q] = o;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      if (col0 + j < N) {
-        const __half h = __float2half_rn(v[j]);
-        orow[col0 + j] = h;
-        m = __vmaxu2(m, abs2_nonan(__half_as_ushort(h)));
-      }
-    }
+  for (int t = 0; t < 16; ++t) {
+    const __half2 h = __halves2half2(__float2half_rn(v[2 * t]), __float2half_rn(v[2 * t + 1]));
+    w[t] = *reinterpret_cast<const uint32_t*>(&h);
+    uint32_t a = abs2_nonan(w[t]);
+    if (2 * t >= valid_cols) a = 0u;
+    else if (2 * t + 1 >= valid_cols) a &= 0xFFFFu;
+    m = __vmaxu2(m, a);
   }
   return max(m & 0xFFFFu, m >> 16);
 }
 
 // ------------------------------------------------------------------- kernel
 
-template <int kEpi, bool kVec>
+template <int kEpi, bool kTmaStore>
 __global__ void __launch_bounds__(THREADS, 1)
 fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
-                const Params p) {
+                const __grid_constant__ CUtensorMap tmap_out, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   SharedStorage& s =
       *reinterpret_cast<SharedStorage*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -339,13 +365,14 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     }
     for (int i = 0; i < NUM_ACC; ++i) {
       mbar_init(&s.acc_full[i], 1);
-      mbar_init(&s.acc_empty[i], 4);  // one arrival per epilogue warp
+      mbar_init(&s.acc_empty[i], EPI_WARPS);  // one arrival per epilogue warp
     }
     mbar_init(&s.drain, 1);
     s.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     prefetch_tmap(&tmap_a);
     prefetch_tmap(&tmap_w);
+    if (kTmaStore) prefetch_tmap(&tmap_out);
   }
   if (warp == 1) {
     tmem_alloc(&s.tmem_base, TMEM_COLS);
@@ -451,26 +478,81 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     }
   } else {
     // --------------------------------------------------------- epilogue
-    const int quarter = warp & 3;  // TMEM lanes this warp may access: 32*quarter ..
+    const int ew = warp - 2;             // 0..7
+    const int quarter = warp & 3;        // TMEM lanes this warp may access: 32*quarter ..
+    const int col_half = ew >> 2;        // which 128 of the 256 accumulator columns
     const float descale = p.alpha * (p.a_scale ? __ldg(p.a_scale) : 1.0f) * (p.w_scale ? __ldg(p.w_scale) : 1.0f);
     uint32_t amax = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
+    int sbuf = 0;  // staging buffer toggle (kTmaStore)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
       if (!mbar_wait(&s.acc_full[acc], acc_phase, abort_flag, p.timeout_ns, SITE_EPI_ACC_FULL)) break;
       tc_fence_after();
       const int m0 = (tile / p.tiles_n) * BM;
-      const int n0 = (tile % p.tiles_n) * BN;
-      const int row = m0 + quarter * 32 + lane;
-      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        if (n0 + c >= p.N) break;  // warp-uniform
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>(c), r);
-        tmem_ld_wait();
-        if (row < p.M) amax = max(amax, epi_chunk<kEpi, kVec>(p, r, row, n0 + c, descale));
+      const int n0 = (tile % p.tiles_n) * BN + col_half * EPI_COLS;
+      const int row0 = m0 + quarter * 32;
+      const int row = row0 + lane;
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN + col_half * EPI_COLS);
+      const int nchunks = min(EPI_COLS / CHUNK, (p.N - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
+      auto process = [&](const uint32_t* regs, int c) {
+        const int col0 = n0 + c * CHUNK;
+        float v[32];
+        epi_values<kEpi, kTmaStore>(p, regs, row, col0, descale, v);
+        uint32_t w[16];
+        const int valid_cols = (row < p.M) ? min(CHUNK, p.N - col0) : 0;
+        amax = max(amax, pack_fp16(v, w, valid_cols));
+        if (kTmaStore) {
+          // Stage [32 rows x 64 B] with the 64-byte swizzle (16-byte chunk index
+          // XOR (row/2)%4), then one lane stores the box with TMA.
+          uint8_t* buf = &s.out[ew][0][0] + sbuf * STAGE_OUT_BYTES;
+          if (lane == 0) bulk_wait_read<1>();  // the store that last read `buf` is done
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk16 = q ^ ((lane >> 1) & 3);
+            *reinterpret_cast<uint4*>(buf + lane * 64 + chunk16 * 16) =
+                make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_out, buf, col0, row0);
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        } else if (row < p.M) {
+          __half* orow = p.out + static_cast<int64_t>(row) * p.N + col0;
+          if (p.out_pairs) {  // even N, 4-byte aligned rows: store fp16 pairs
+            uint32_t* o32 = reinterpret_cast<uint32_t*>(orow);
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+              if (2 * t + 1 < valid_cols) o32[t] = w[t];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < valid_cols)
+                orow[j] = __ushort_as_half(static_cast<unsigned short>((w[j >> 1] >> ((j & 1) * 16)) & 0xFFFFu));
+          }
+        }
+      };
+      // Double-buffered TMEM drain: the load of chunk c+1 is in flight while chunk c is processed.
+      uint32_t ra[32], rb[32];
+      if (nchunks > 0) {
+        tmem_ld_32x32b_x32(taddr, ra);
+        tmem_ld_wait(ra);
       }
+      if (nchunks > 1) tmem_ld_32x32b_x32(taddr + 1 * CHUNK, rb);
+      if (nchunks > 0) process(ra, 0);
+      if (nchunks > 1) tmem_ld_wait(rb);
+      if (nchunks > 2) tmem_ld_32x32b_x32(taddr + 2 * CHUNK, ra);
+      if (nchunks > 1) process(rb, 1);
+      if (nchunks > 2) tmem_ld_wait(ra);
+      if (nchunks > 3) tmem_ld_32x32b_x32(taddr + 3 * CHUNK, rb);
+      if (nchunks > 2) process(ra, 2);
+      if (nchunks > 3) tmem_ld_wait(rb);
+      if (nchunks > 3) process(rb, 3);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
@@ -479,6 +561,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         acc_phase ^= 1u;
       }
     }
+    if (kTmaStore && lane == 0) bulk_wait_all();  // all of this warp's stores have landed
     if (p.out_amax != nullptr) {
       amax = warp_max_u32(amax);
       if (lane == 0 && amax != 0u) atomicMax(p.out_amax, amax);
@@ -521,17 +604,18 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 2-D uint8 tensor map: inner dim K (contiguous), outer dim rows, 128B swizzle.
-int make_tmap(CUtensorMap* map, const void* base, uint64_t k, uint64_t rows, uint32_t box_rows) {
+// 2-D tensor map, inner dim contiguous.
+int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes, const void* base, uint64_t inner,
+              uint64_t outer, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
   auto encode = get_encode_fn();
   if (encode == nullptr) return fail(WBK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
-  const cuuint64_t dims[2] = {k, rows};
-  const cuuint64_t strides[1] = {k};
-  const cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), box_rows};
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * elem_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
   const cuuint32_t estr[2] = {1, 1};
-  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  const CUresult r = encode(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(WBK_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
   return WBK_OK;
 }
@@ -545,8 +629,9 @@ uint64_t wait_timeout_ns() {
   return t;
 }
 
-template <int kEpi, bool kVec>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const Params& p, int grid, cudaStream_t stream) {
+template <int kEpi, bool kTma>
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const Params& p, int grid,
+                cudaStream_t stream) {
   static std::mutex mu;
   static std::vector<char> configured;
   const int dev = current_device();
@@ -555,7 +640,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const Params& p, i
     std::lock_guard<std::mutex> lock(mu);
     if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
     if (!configured[dev]) {
-      if (int e = cuda_check(cudaFuncSetAttribute(fp8_gemm_kernel<kEpi, kVec>,
+      if (int e = cuda_check(cudaFuncSetAttribute(fp8_gemm_kernel<kEpi, kTma>,
                                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                   static_cast<int>(SMEM_BYTES)),
                              "cudaFuncSetAttribute(max dynamic smem)"))
@@ -563,13 +648,14 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const Params& p, i
       configured[dev] = 1;
     }
   }
-  fp8_gemm_kernel<kEpi, kVec><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tw, p);
+  fp8_gemm_kernel<kEpi, kTma><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tw, to, p);
   return cuda_check(cudaGetLastError(), "fp8 gemm launch");
 }
 
 template <int kEpi>
-int dispatch_vec(bool vec, const CUtensorMap& ta, const CUtensorMap& tw, const Params& p, int grid, cudaStream_t s) {
-  return vec ? launch_gemm<kEpi, true>(ta, tw, p, grid, s) : launch_gemm<kEpi, false>(ta, tw, p, grid, s);
+int dispatch_store(bool tma, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const Params& p,
+                   int grid, cudaStream_t s) {
+  return tma ? launch_gemm<kEpi, true>(ta, tw, to, p, grid, s) : launch_gemm<kEpi, false>(ta, tw, to, p, grid, s);
 }
 
 }  // namespace
@@ -600,9 +686,18 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, 
   if (!aligned(out, 2) || (bias && !aligned(bias, 2)) || (residual && !aligned(residual, 2)))
     return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: fp16 pointers must be 2-byte aligned");
 
-  CUtensorMap ta, tw;
-  if (int e = make_tmap(&ta, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), BM)) return e;
-  if (int e = make_tmap(&tw, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), BN)) return e;
+  // TMA store and vector loads need 16-byte aligned rows: N % 8 == 0 and aligned bases.
+  const bool vec = (N % 8 == 0) && aligned(out, 16) && (!bias || aligned(bias, 16)) && (!residual || aligned(residual, 16));
+
+  CUtensorMap ta, tw, to;
+  if (int e = make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
+  if (int e = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, K, N, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
+  if (vec) {
+    if (int e = make_tmap(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, out, N, M, CHUNK, 32, CU_TENSOR_MAP_SWIZZLE_64B))
+      return e;
+  } else {
+    to = ta;  // unused by the direct-store kernel
+  }
 
   Params p;
   p.M = static_cast<int>(M);
@@ -621,21 +716,21 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, 
   p.residual = static_cast<const __half*>(residual);
   p.out = static_cast<__half*>(out);
   p.out_amax = out_amax_bits;
+  p.out_pairs = (N % 2 == 0) && aligned(out, 4);
   // Instruction descriptor (kind::f8f6f4): D fp32 [4,6)=1; A format [7,10);
   // B format [10,13); both K-major (bits 15,16 = 0); N>>3 [17,23); M>>4 [24,29).
   p.idesc = (1u << 4) | (static_cast<uint32_t>(a_fmt) << 7) | (static_cast<uint32_t>(w_fmt) << 10) |
             (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
   p.timeout_ns = wait_timeout_ns();
 
-  const bool vec = (N % 8 == 0) && aligned(out, 16) && (!bias || aligned(bias, 16)) && (!residual || aligned(residual, 16));
   const int sms = sm_count() > 0 ? sm_count() : 148;
   const int grid = static_cast<int>(num_tiles < sms ? num_tiles : sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   switch (epilogue) {
-    case WBK_EPI_NONE: return dispatch_vec<WBK_EPI_NONE>(vec, ta, tw, p, grid, s);
-    case WBK_EPI_GELU: return dispatch_vec<WBK_EPI_GELU>(vec, ta, tw, p, grid, s);
-    case WBK_EPI_RESIDUAL: return dispatch_vec<WBK_EPI_RESIDUAL>(vec, ta, tw, p, grid, s);
-    default: return dispatch_vec<WBK_EPI_RESIDUAL_CLAMP>(vec, ta, tw, p, grid, s);
+    case WBK_EPI_NONE: return dispatch_store<WBK_EPI_NONE>(vec, ta, tw, to, p, grid, s);
+    case WBK_EPI_GELU: return dispatch_store<WBK_EPI_GELU>(vec, ta, tw, to, p, grid, s);
+    case WBK_EPI_RESIDUAL: return dispatch_store<WBK_EPI_RESIDUAL>(vec, ta, tw, to, p, grid, s);
+    default: return dispatch_store<WBK_EPI_RESIDUAL_CLAMP>(vec, ta, tw, to, p, grid, s);
   }
 }
 

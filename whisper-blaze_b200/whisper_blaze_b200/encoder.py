@@ -189,30 +189,45 @@ class FP8EncoderStack:
         self.attn.view(B, S, H, Dh).copy_(o)
         return self.attn
 
-    def _layer(self, L: _QuantLayer, h: torch.Tensor, h_next: torch.Tensor, B: int, S: int) -> None:
+    def _layer(self, L: _QuantLayer, h: torch.Tensor, h_next: torch.Tensor, B: int, S: int,
+               capture: Optional[dict] = None) -> None:
         cfg = self.cfg
         T, D, Fd = B * S, cfg.d_model, cfg.ffn
         amax, sc = self.amax, self.scales
+        keep = (lambda k, t: capture.__setitem__(k, t.clone())) if capture is not None else (lambda k, t: None)
         amax.zero_()
         ops.layernorm(h, None, L.ln1_g, L.ln1_b, cfg.eps, out=self.x, out_amax=amax[0:1])
         ops.quantise_from_amax(self.x, amax[0:1], q_out=self.xq, scale_out=sc[0:1])
+        keep("ln1", self.x), keep("ln1_q", self.xq), keep("ln1_s", sc[0:1])
         self._gemm("qkv", 2 * T * D * 3 * D, self.xq, sc[0:1], L.w_qkv, L.s_qkv, L.b_qkv, out=self.qkv)
+        keep("qkv", self.qkv)
         attn = self._attention(B, S)
         ops.amax_accumulate(attn, amax[1:2])
         ops.quantise_from_amax(attn, amax[1:2], q_out=self.aq, scale_out=sc[1:2])
+        keep("attn", attn), keep("attn_q", self.aq), keep("attn_s", sc[1:2])
         self._gemm("out_proj", 2 * T * D * D, self.aq, sc[1:2], L.w_o, L.s_o, L.b_o, residual=h,
                    epilogue="residual", out=self.h2)
+        keep("h2", self.h2)
         ops.layernorm(self.h2, None, L.ln2_g, L.ln2_b, cfg.eps, out=self.x, out_amax=amax[2:3])
         ops.quantise_from_amax(self.x, amax[2:3], q_out=self.xq, scale_out=sc[2:3])
+        keep("ln2", self.x), keep("ln2_q", self.xq), keep("ln2_s", sc[2:3])
         self._gemm("fc1", 2 * T * D * Fd, self.xq, sc[2:3], L.w_fc1, L.s_fc1, L.b_fc1, epilogue="gelu",
                    out=self.f, out_amax=amax[3:4])
         ops.quantise_from_amax(self.f, amax[3:4], q_out=self.fq, scale_out=sc[3:4])
+        keep("fc1", self.f), keep("fc1_q", self.fq), keep("fc1_s", sc[3:4])
         self._gemm("fc2", 2 * T * Fd * D, self.fq, sc[3:4], L.w_fc2, L.s_fc2, L.b_fc2, residual=self.h2,
                    epilogue="residual_clamp", out=h_next)
+        keep("out", h_next)
 
     @torch.inference_mode()
-    def forward(self, hidden: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        """hidden [B, S, D] fp16 on this stack's device -> [B, S, D] fp16 (the final LayerNorm applied)."""
+    def forward(self, hidden: torch.Tensor, out: Optional[torch.Tensor] = None,
+                capture: Optional[List[dict]] = None) -> torch.Tensor:
+        """hidden [B, S, D] fp16 on this stack's device -> [B, S, D] fp16 (the final LayerNorm applied).
+
+        capture: if a list is given, one dict per layer of copies of that
+        layer's intermediates (LN outputs, fp8 codes and scales, qkv,
+        attention, fc1, residual sums) is appended — for stage-wise parity
+        checks; it costs copies, so it is off on the production path."""
         ops.require_input(hidden, "hidden")
         ops.require_fp16(hidden, "hidden")
         B, S, D = hidden.shape
@@ -225,7 +240,11 @@ class FP8EncoderStack:
             bufs = (self.h_a, self.h_b)
             for i, L in enumerate(self.layers):
                 nxt = bufs[i % 2]
-                self._layer(L, h, nxt, B, S)
+                cap = None
+                if capture is not None:
+                    cap = {"in": h.clone()}
+                    capture.append(cap)
+                self._layer(L, h, nxt, B, S, cap)
                 h = nxt
             o = self.out if out is None else out.view(T, D)
             ops.layernorm(h, None, self.final_g, self.final_b, self.cfg.eps, out=o)

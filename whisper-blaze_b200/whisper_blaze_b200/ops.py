@@ -17,6 +17,15 @@ from ._lib import (EPI_GELU, EPI_NONE, EPI_RESIDUAL, EPI_RESIDUAL_CLAMP, FMT_E4M
 
 Scale = Union[float, torch.Tensor]
 
+# Number of libwbk kernels launched by this process (quantise() launches the
+# amax and the quantise kernel, 2; every other op launches 1).
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
 _FMT_BY_NAME = {"e4m3": FMT_E4M3, "e5m2": FMT_E5M2, FMT_E4M3: FMT_E4M3, FMT_E5M2: FMT_E5M2}
 _EPI_BY_NAME = {"none": EPI_NONE, "bias": EPI_NONE, "gelu": EPI_GELU, "residual": EPI_RESIDUAL,
                 "residual_clamp": EPI_RESIDUAL_CLAMP, EPI_NONE: EPI_NONE, EPI_GELU: EPI_GELU,
@@ -75,6 +84,7 @@ def amax_accumulate(x: torch.Tensor, amax_ws: torch.Tensor) -> torch.Tensor:
     require_same_device(x, amax_ws)
     with torch.cuda.device(x.device):
         check(lib().wbk_amax_f16(x.data_ptr(), x.numel(), amax_ws.data_ptr(), stream_of(x)), "amax")
+    _count()
     return amax_ws
 
 
@@ -90,6 +100,7 @@ def quantise_from_amax(x: torch.Tensor, amax_ws: torch.Tensor, fmt="e4m3", q_out
     with torch.cuda.device(x.device):
         check(lib().wbk_quantise_from_amax_f16(x.data_ptr(), x.numel(), f, amax_ws.data_ptr(), q.data_ptr(),
                                                s.data_ptr(), stream_of(x)), "quantise")
+    _count()
     return q, s
 
 
@@ -107,6 +118,7 @@ def quantise(x: torch.Tensor, fmt="e4m3", q_out: Optional[torch.Tensor] = None,
     with torch.cuda.device(x.device):
         check(lib().wbk_quantise_f16(x.data_ptr(), x.numel(), f, q.data_ptr(), s.data_ptr(), ws.data_ptr(),
                                      stream_of(x)), "quantise")
+    _count(2)
     return q, s
 
 
@@ -121,6 +133,7 @@ def dequantise(q: torch.Tensor, scale: float, shape: Sequence[int], fmt="e4m3") 
     with torch.cuda.device(q.device):
         check(lib().wbk_dequantise_f16(q.data_ptr(), q.numel(), f, float(scale), out.data_ptr(), stream_of(q)),
               "dequantise")
+    _count()
     return out
 
 
@@ -153,6 +166,7 @@ def layernorm(x: torch.Tensor, residual: Optional[torch.Tensor], gamma: torch.Te
     with torch.cuda.device(x.device):
         check(lib().wbk_layernorm_f16(x.data_ptr(), ptr(residual), gamma.data_ptr(), beta.data_ptr(), o.data_ptr(),
                                       ptr(s), rows, D, float(eps), ptr(out_amax), stream_of(x)), "layernorm_fused")
+    _count()
     return o, s
 
 
@@ -173,6 +187,7 @@ def rmsnorm(x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor, eps: f
     with torch.cuda.device(x.device):
         check(lib().wbk_rmsnorm_f16(x.data_ptr(), residual.data_ptr(), gamma.data_ptr(), out.data_ptr(),
                                     x.numel() // D, D, float(eps), stream_of(x)), "rmsnorm_fused")
+    _count()
     return out
 
 
@@ -233,4 +248,5 @@ def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
         check(lib().wbk_gemm_fp8(a.data_ptr(), w.data_ptr(), M, N, K, fmt_code(a_format), fmt_code(w_format), alpha,
                                  pa, pw, ptr(bias), ptr(residual), o.data_ptr(), epi, ptr(out_amax), stream_of(a)),
               "gemm_fp8")
+    _count()
     return o
