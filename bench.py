@@ -256,12 +256,14 @@ def run_stack(args, world, rank, local):
     with ClockSampler(local) as clocks:
         barrier(world)
         torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStart()  # profiler capture window = timed steps (no-op unprofiled)
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for _ in range(args.steps):
             step()
         t1.record(stream)
         torch.cuda.synchronize()
+        torch.cuda.cudart().cudaProfilerStop()
         barrier(world)
     launches = ops.LAUNCHES[0] - launches0
     ms_local = t0.elapsed_time(t1) / args.steps
