@@ -94,6 +94,27 @@ int wbk_quantise_from_amax_f16(const void* x, int64_t n, int fmt,
 int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out,
                      float* scale_out, uint32_t* amax_ws, wbk_stream_t stream);
 
+/* Same result as wbk_quantise_f16 (bit for bit), for callers that cannot
+ * allocate device memory: code running where cudaMalloc is forbidden or must
+ * not be called (a host callback or real-time audio thread with a
+ * no-allocation rule, a plugin whose host owns every device allocation, a
+ * driver path that must not fail on allocation). It takes no amax_ws; its
+ * scratch is a file-scope static device array of 4096 words (16 KB, held on
+ * every GPU that loads libwbk until the process exits): per-CTA partial
+ * maxima, one CTA per 65536 elements, plus the final amax.
+ * Limit: n <= 268369920 elements (4095 CTAs); larger n returns
+ * WBK_ERR_UNSUPPORTED with a message, before anything is launched.
+ * The first call on a device looks up the array's device address (with that
+ * device current) and caches it; make that first call before any stream
+ * capture. Every call shares the one array and rewrites every word it reads
+ * (nothing needs to start at zero); calls that overlap on the GPU, e.g. on
+ * two streams at once, race on it. Allocates nothing: no cudaMalloc, no
+ * cudaFree, no allocating library routine.
+ * No counterpart in the reference (its quantiser allocates a per-call
+ * torch::zeros buffer, csrc/kernels/fp8_quantize.cu:201). */
+int wbk_quantise_f16_noalloc(const void* x, int64_t n, int fmt, void* q_out,
+                             float* scale_out, wbk_stream_t stream);
+
 /* out = fp16(float(q) * scale) for n fp8 values; scale is a host float.
  * Replaces: dequantise_e4m3_to_fp16_kernel / _e5m2, fp8_quantize.cu:143-187,
  * and dequantise_e4m3 / dequantise_e5m2, fp8_quantize.cu:260-291. */

@@ -11,6 +11,9 @@
 // Layout in HBM: the input is a flat fp16 array (any shape, contiguous); the
 // output is a flat uint8 array of the same element count. Each thread moves
 // 8 elements per step: one 16-byte load in, one 8-byte store out.
+#include <mutex>
+#include <vector>
+
 #include "wbk_common.cuh"
 
 namespace wbk {
@@ -182,6 +185,95 @@ int check_fmt(int fmt) {
   return WBK_OK;
 }
 
+// ------------------------------------------------- no-allocation quantise
+//
+// For callers that cannot allocate device memory themselves (code that runs
+// where cudaMalloc is not allowed or not wanted, e.g. inside a host callback,
+// a real-time audio thread with a no-allocation rule, or a plugin host that
+// owns every device allocation), wbk_quantise_f16_noalloc keeps its scratch
+// in this file-scope array instead of asking for an amax_ws buffer:
+//   word 0           the tensor's amax (fp16 bits), written by the finalize kernel;
+//   words 1..4095    one partial max per CTA of the amax pass, one CTA per
+//                    kNoAllocElemsPerCta elements.
+// Every GPU that loads libwbk holds these 16 KB until the process exits.
+// Every word a call reads is written earlier in the same call, so nothing
+// needs clearing; calls that overlap on the GPU (different streams at the
+// same time) share the array and race.
+constexpr int kNoAllocWords = 4096;
+constexpr int kNoAllocMaxCtas = kNoAllocWords - 1;
+constexpr int64_t kNoAllocElemsPerCta = 65536;  // 256 threads x 32 vectors of 8 halves
+constexpr int64_t kNoAllocMaxElems = kNoAllocElemsPerCta * kNoAllocMaxCtas;
+static __device__ __align__(256) uint32_t g_noalloc_scratch[kNoAllocWords];
+
+// CTA b writes max|x| (fp16 bits, NaN ignored) over elements
+// [b*kNoAllocElemsPerCta, (b+1)*kNoAllocElemsPerCta) to partials[b].
+template <bool kVec>
+__global__ void __launch_bounds__(kThreads)
+amax_partials_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ partials) {
+  const int64_t begin = static_cast<int64_t>(blockIdx.x) * kNoAllocElemsPerCta;
+  const int64_t end = min(n, begin + kNoAllocElemsPerCta);
+  uint32_t m = 0;
+  int64_t done = begin;
+  if (kVec) {
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    const int64_t vbegin = begin >> 3, vend = end >> 3;
+    for (int64_t i = vbegin + threadIdx.x; i < vend; i += kThreads) {
+      const uint4 v = ld_stream16(xv + i);
+      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v.x), abs2_nonan(v.y)),
+                               __vmaxu2(abs2_nonan(v.z), abs2_nonan(v.w))));
+    }
+    done = vend << 3;
+  }
+  const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
+  for (int64_t i = done + threadIdx.x; i < end; i += kThreads) m = __vmaxu2(m, abs2_nonan(xs[i]));
+  uint32_t mm = warp_max_u32(max(m & 0xFFFFu, m >> 16));
+  __shared__ uint32_t red[kThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = mm;
+  __syncthreads();
+  if (warp == 0) {
+    mm = warp_max_u32(lane < kThreads / 32 ? red[lane] : 0u);
+    if (lane == 0) partials[blockIdx.x] = mm;
+  }
+}
+
+// One CTA: *amax_bits = max(partials[0..count)).
+__global__ void __launch_bounds__(kThreads)
+amax_finalize_kernel(const uint32_t* __restrict__ partials, int count, uint32_t* __restrict__ amax_bits) {
+  uint32_t m = 0;
+  for (int i = threadIdx.x; i < count; i += kThreads) m = max(m, partials[i]);
+  m = warp_max_u32(m);
+  __shared__ uint32_t red[kThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  if (warp == 0) {
+    m = warp_max_u32(lane < kThreads / 32 ? red[lane] : 0u);
+    if (lane == 0) *amax_bits = m;
+  }
+}
+
+// Device address of g_noalloc_scratch for the current device. The host-side
+// name is only a stand-in, so the address is looked up once per device (with
+// that device current) and cached.
+int noalloc_scratch(uint32_t** out) {
+  static std::mutex mu;
+  static std::vector<uint32_t*> cache;
+  const int dev = current_device();
+  if (dev < 0) return fail(WBK_ERR_CUDA, "wbk_quantise_f16_noalloc: no current CUDA device");
+  std::lock_guard<std::mutex> lock(mu);
+  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, nullptr);
+  if (cache[dev] == nullptr) {
+    uint32_t* ptr = nullptr;
+    if (int e = cuda_check(cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch),
+                           "wbk_quantise_f16_noalloc: cudaGetSymbolAddress(scratch)"))
+      return e;
+    cache[dev] = ptr;
+  }
+  *out = cache[dev];
+  return WBK_OK;
+}
+
 }  // namespace
 }  // namespace wbk
 
@@ -253,6 +345,32 @@ int wbk_dequantise_f16(const void* q, int64_t n, int fmt, float scale, void* out
     else dequantise_f16_kernel<WBK_FMT_E5M2, false><<<grid, kThreads, 0, s>>>(qq, n, scale, o);
   }
   return cuda_check(cudaGetLastError(), "wbk_dequantise_f16 launch");
+}
+
+int wbk_quantise_f16_noalloc(const void* x, int64_t n, int fmt, void* q_out, float* scale_out,
+                             wbk_stream_t stream) {
+  if (int e = check_fmt(fmt)) return e;
+  if (n < 0) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_f16_noalloc: n < 0");
+  if (n > kNoAllocMaxElems)
+    return fail(WBK_ERR_UNSUPPORTED,
+                "wbk_quantise_f16_noalloc: n = %lld elements exceeds the limit of %lld set by its static scratch "
+                "(%d words); use wbk_quantise_f16 with a caller-provided amax_ws for larger tensors",
+                (long long)n, (long long)kNoAllocMaxElems, kNoAllocWords);
+  if (n > 0 && (x == nullptr || q_out == nullptr))
+    return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_f16_noalloc: null pointer");
+  uint32_t* scratch = nullptr;
+  if (int e = noalloc_scratch(&scratch)) return e;
+  uint32_t* amax_word = scratch;
+  uint32_t* partials = scratch + 1;
+  const int ctas = static_cast<int>(n == 0 ? 1 : (n + kNoAllocElemsPerCta - 1) / kNoAllocElemsPerCta);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __half* xh = static_cast<const __half*>(x);
+  if (aligned(x, 16)) amax_partials_kernel<true><<<ctas, kThreads, 0, s>>>(xh, n, partials);
+  else amax_partials_kernel<false><<<ctas, kThreads, 0, s>>>(xh, n, partials);
+  if (int e = cuda_check(cudaGetLastError(), "wbk_quantise_f16_noalloc amax launch")) return e;
+  amax_finalize_kernel<<<1, kThreads, 0, s>>>(partials, ctas, amax_word);
+  if (int e = cuda_check(cudaGetLastError(), "wbk_quantise_f16_noalloc finalize launch")) return e;
+  return wbk_quantise_from_amax_f16(x, n, fmt, amax_word, q_out, scale_out, stream);
 }
 
 }  // extern "C"

@@ -41,6 +41,7 @@ _PROTOTYPES = {
     "wbk_amax_f16": (_i32, [_vp, _i64, _vp, _vp]),
     "wbk_quantise_from_amax_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "wbk_quantise_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
+    "wbk_quantise_f16_noalloc": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp]),
     "wbk_dequantise_f16": (_i32, [_vp, _i64, _i32, _f32, _vp, _vp]),
     "wbk_layernorm_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp]),
     "wbk_rmsnorm_f16": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
