@@ -271,6 +271,13 @@ def run_stack(args, world, rank, local):
     gemm_ms = sum(t.ms() for t in stack.gemm_timings)
     gemm_flops = sum(t.flops for t in stack.gemm_timings)
     n_gemm = len(stack.gemm_timings)
+    breakdown = {}
+    for t in stack.gemm_timings:
+        b = breakdown.setdefault(t.name, {"ms": 0.0, "flops": 0.0})
+        b["ms"] += t.ms()
+        b["flops"] += t.flops
+    breakdown = {k: {"ms_per_step": v["ms"] / args.steps, "tflops": v["flops"] / (v["ms"] * 1e-3) / 1e12}
+                 for k, v in breakdown.items()}
     stack.gemm_timings = None
     clock_info = clocks.summary()
 
@@ -332,6 +339,7 @@ def run_stack(args, world, rank, local):
                          "frac_of_nominal_fp8_4500": (achieved / NOMINAL_FP8_TFLOPS) if achieved else None,
                          "gemm_launches_timed": n_gemm, "gemm_ms_per_step": gemm_ms / args.steps,
                          "gemm_share_of_step": (gemm_ms / args.steps) / ms_local,
+                         "gemm_breakdown": breakdown,
                          "traffic": roofline_traffic("fp8_gemm_stack")},
             "gpu_launches": launches,
             "clocks": clock_info,
