@@ -310,22 +310,45 @@ __device__ __forceinline__ void add_halves8(float* v, const uint4& raw) {
   }
 }
 
+constexpr bool has_residual(int epi) { return epi == WBK_EPI_RESIDUAL || epi == WBK_EPI_RESIDUAL_CLAMP; }
+
+// Issues the residual loads of one full 32-column chunk of this thread's row
+// (4 x 16 B) so they are in flight while the previous chunk is processed.
+// Partial chunks and rows >= M are handled by the scalar path in epi_values.
+template <int kEpi, bool kVec>
+__device__ __forceinline__ void prefetch_residual(const Params& p, int row, int col0, uint4* r) {
+  if (has_residual(kEpi) && kVec && row < p.M && col0 + 32 <= p.N) {
+    const uint4* rv = reinterpret_cast<const uint4*>(p.residual + static_cast<int64_t>(row) * p.N + col0);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) r[q] = __ldg(rv + q);
+  }
+}
+
 // fp32 accumulators of one 32-column chunk of this thread's row -> epilogue
 // values in fp32 (descale, bias, activation, residual, clamp). Columns >= N
 // and rows >= M are never read from global memory.
 template <int kEpi, bool kVec>
-__device__ __forceinline__ void epi_values(const Params& p, const uint32_t* acc, int row, int col0, float descale,
-                                           float* v) {
+__device__ __forceinline__ void epi_values(const Params& p, const uint32_t* acc, const uint4* res, int row, int col0,
+                                           float descale, float* v) {
   const int N = p.N;
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]) * descale;
   const bool full = kVec && (col0 + 32 <= N);
-  if (p.bias != nullptr) {
-    if (full) {
-      const uint4* bv = reinterpret_cast<const uint4*>(p.bias + col0);
+  if (p.bias != nullptr && full) {
+    const uint4* bv = reinterpret_cast<const uint4*>(p.bias + col0);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) add_halves8(v + 8 * q, __ldg(bv + q));
-    } else {
+    for (int q = 0; q < 4; ++q) {
+      const uint4 b = __ldg(bv + q);
+      const __half2* h = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float2 f = __half22float2(h[t]);
+        v[8 * q + 2 * t] = fmaf(__uint_as_float(acc[8 * q + 2 * t]), descale, f.x);
+        v[8 * q + 2 * t + 1] = fmaf(__uint_as_float(acc[8 * q + 2 * t + 1]), descale, f.y);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(acc[j]) * descale;
+    if (p.bias != nullptr) {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
         if (col0 + j < N) v[j] += __half2float(p.bias[col0 + j]);
@@ -333,14 +356,13 @@ __device__ __forceinline__ void epi_values(const Params& p, const uint32_t* acc,
   }
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = epi_apply<kEpi>(v[j]);
-  if (kEpi == WBK_EPI_RESIDUAL || kEpi == WBK_EPI_RESIDUAL_CLAMP) {
+  if (has_residual(kEpi)) {
     if (row < p.M) {
-      const __half* rrow = p.residual + static_cast<int64_t>(row) * N;
       if (full) {
-        const uint4* rv = reinterpret_cast<const uint4*>(rrow + col0);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) add_halves8(v + 8 * q, __ldg(rv + q));
+        for (int q = 0; q < 4; ++q) add_halves8(v + 8 * q, res[q]);
       } else {
+        const __half* rrow = p.residual + static_cast<int64_t>(row) * N;
 #pragma unroll
         for (int j = 0; j < 32; ++j)
           if (col0 + j < N) v[j] += __half2float(rrow[col0 + j]);
@@ -353,19 +375,27 @@ __device__ __forceinline__ void epi_values(const Params& p, const uint32_t* acc,
   }
 }
 
-// Rounds v to fp16 into 16 packed words; returns max|fp16| over valid columns.
-__device__ __forceinline__ uint32_t pack_fp16(const float* v, uint32_t* w, int valid_cols) {
-  uint32_t m = 0;
+// Rounds v to fp16 into 16 packed words.
+__device__ __forceinline__ void pack_fp16(const float* v, uint32_t* w) {
 #pragma unroll
   for (int t = 0; t < 16; ++t) {
-    const __half2 h = __halves2half2(__float2half_rn(v[2 * t]), __float2half_rn(v[2 * t + 1]));
+    const __half2 h = __floats2half2_rn(v[2 * t], v[2 * t + 1]);
     w[t] = *reinterpret_cast<const uint32_t*>(&h);
-    uint32_t a = abs2_nonan(w[t]);
-    if (2 * t >= valid_cols) a = 0u;
-    else if (2 * t + 1 >= valid_cols) a &= 0xFFFFu;
-    m = __vmaxu2(m, a);
   }
-  return max(m & 0xFFFFu, m >> 16);
+}
+
+// Running max of |v| over the valid columns (fmaxf ignores NaN). Rounding to
+// fp16 is monotone and symmetric, so fp16(max |v|) is max |fp16(v)|.
+__device__ __forceinline__ float absmax_valid(float m, const float* v, int valid_cols) {
+  if (valid_cols >= 32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(v[j]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid_cols) m = fmaxf(m, fabsf(v[j]));
+  }
+  return m;
 }
 
 // ------------------------------------------------------------------- kernel
@@ -505,27 +535,30 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     const int quarter = warp & 3;        // TMEM lanes this warp may access: 32*quarter ..
     const int col_half = ew >> 2;        // which 128 of the 256 accumulator columns
     const float descale = p.alpha * (p.a_scale ? __ldg(p.a_scale) : 1.0f) * (p.w_scale ? __ldg(p.w_scale) : 1.0f);
-    uint32_t amax = 0;
+    float amax = 0.0f;
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;  // staging buffer toggle (kTmaStore)
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-      if (!mbar_wait(&s.acc_full[acc], acc_phase, abort_flag, p.timeout_ns, SITE_EPI_ACC_FULL)) break;
-      tc_fence_after();
       const int m0 = (tile / p.tiles_n) * BM;
       const int n0 = (tile % p.tiles_n) * BN + col_half * EPI_COLS;
       const int row0 = m0 + quarter * 32;
       const int row = row0 + lane;
+      uint4 resa[4], resb[4];
+      prefetch_residual<kEpi, kTmaStore>(p, row, n0, resa);  // overlaps the tile's MMAs
+      if (!mbar_wait(&s.acc_full[acc], acc_phase, abort_flag, p.timeout_ns, SITE_EPI_ACC_FULL)) break;
+      tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * BN + col_half * EPI_COLS);
       const int nchunks = min(EPI_COLS / CHUNK, (p.N - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
-      auto process = [&](const uint32_t* regs, int c) {
+      auto process = [&](const uint32_t* regs, const uint4* res, int c) {
         const int col0 = n0 + c * CHUNK;
         float v[32];
-        epi_values<kEpi, kTmaStore>(p, regs, row, col0, descale, v);
-        uint32_t w[16];
+        epi_values<kEpi, kTmaStore>(p, regs, res, row, col0, descale, v);
         const int valid_cols = (row < p.M) ? min(CHUNK, p.N - col0) : 0;
-        amax = max(amax, pack_fp16(v, w, valid_cols));
+        amax = absmax_valid(amax, v, valid_cols);
+        uint32_t w[16];
+        pack_fp16(v, w);
         if (kTmaStore) {
           // Stage [32 rows x 64 B] with the 64-byte swizzle (16-byte chunk index
           // XOR (row/2)%4), then one lane stores the box with TMA.
@@ -560,22 +593,31 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
           }
         }
       };
-      // Double-buffered TMEM drain: the load of chunk c+1 is in flight while chunk c is processed.
+      // Double-buffered drain: the TMEM load and the residual loads of chunk c+1
+      // are in flight while chunk c is processed.
       uint32_t ra[32], rb[32];
       if (nchunks > 0) {
         tmem_ld_32x32b_x32(taddr, ra);
         tmem_ld_wait(ra);
       }
-      if (nchunks > 1) tmem_ld_32x32b_x32(taddr + 1 * CHUNK, rb);
-      if (nchunks > 0) process(ra, 0);
-      if (nchunks > 1) tmem_ld_wait(rb);
-      if (nchunks > 2) tmem_ld_32x32b_x32(taddr + 2 * CHUNK, ra);
-      if (nchunks > 1) process(rb, 1);
-      if (nchunks > 2) tmem_ld_wait(ra);
-      if (nchunks > 3) tmem_ld_32x32b_x32(taddr + 3 * CHUNK, rb);
-      if (nchunks > 2) process(ra, 2);
-      if (nchunks > 3) tmem_ld_wait(rb);
-      if (nchunks > 3) process(rb, 3);
+#pragma unroll 1
+      for (int c = 0; c < nchunks; c += 2) {
+        const bool more1 = c + 1 < nchunks, more2 = c + 2 < nchunks;
+        if (more1) {
+          tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>((c + 1) * CHUNK), rb);
+          prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 1) * CHUNK, resb);
+        }
+        process(ra, resa, c);
+        if (more1) {
+          tmem_ld_wait(rb);
+          if (more2) {
+            tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>((c + 2) * CHUNK), ra);
+            prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 2) * CHUNK, resa);
+          }
+          process(rb, resb, c + 1);
+          if (more2) tmem_ld_wait(ra);
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
@@ -586,8 +628,8 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     }
     if (kTmaStore && lane == 0) bulk_wait_all();  // all of this warp's stores have landed
     if (p.out_amax != nullptr) {
-      amax = warp_max_u32(amax);
-      if (lane == 0 && amax != 0u) atomicMax(p.out_amax, amax);
+      const uint32_t bits = warp_max_u32(__half_as_ushort(__float2half_rn(amax)));
+      if (lane == 0 && bits != 0u) atomicMax(p.out_amax, bits);
     }
   }
 
