@@ -44,6 +44,8 @@ typedef struct CUstream_st* wbk_stream_t;
 #define WBK_EPI_GELU          1   /* out = fp16(gelu_erf(acc*descale + bias)) */
 #define WBK_EPI_RESIDUAL      2   /* out = fp16(acc*descale + bias + residual) */
 #define WBK_EPI_RESIDUAL_CLAMP 3  /* as RESIDUAL, then clamp to +-(65504-1000) (HF fp16 encoder clamp) */
+#define WBK_EPI_BIAS_MAXKEY   4   /* as NONE; out_amax_bits (required) max-accumulates the order key of the
+                                     largest fp16 output, for wbk_quantise_gelu_f16 */
 
 /* ---------------------------------------------------------------- misc */
 
@@ -114,6 +116,20 @@ int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out,
  * torch::zeros buffer, csrc/kernels/fp8_quantize.cu:201). */
 int wbk_quantise_f16_noalloc(const void* x, int64_t n, int fmt, void* q_out,
                              float* scale_out, wbk_stream_t stream);
+
+/* FFN activation quantiser: g = fp16(gelu_erf(float(y))) for n fp16 values y
+ * (the fc1 output), then the per-tensor quantise of g exactly as
+ * wbk_quantise_f16 does it (scale from max|g|). g itself is not stored.
+ * ymax_key (may be NULL): the key of the largest y written by a GEMM with the
+ * WBK_EPI_BIAS_MAXKEY epilogue; when gelu(y_max) >= 0.171 the amax of g is
+ * taken from it (exact: GELU is increasing above -0.7518 and |GELU| < 0.17
+ * below), otherwise one pass computes it. amax_ws: caller-owned device uint32.
+ * gelu_erf uses the erf of Abramowitz & Stegun 7.1.26 (|error| <= 1.5e-7).
+ * Replaces: HF's GELU on the fp16 fc1 output followed by quantise_e4m3 of it
+ * (whisper_blaze/model.py:93-96 applied to the fc2 input). */
+int wbk_quantise_gelu_f16(const void* y, int64_t n, int fmt, const uint32_t* ymax_key,
+                          void* q_out, float* scale_out, uint32_t* amax_ws,
+                          wbk_stream_t stream);
 
 /* out = fp16(float(q) * scale) for n fp8 values; scale is a host float.
  * Replaces: dequantise_e4m3_to_fp16_kernel / _e5m2, fp8_quantize.cu:143-187,

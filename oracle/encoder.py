@@ -10,8 +10,9 @@ and of the weight, fp32 matmul of the dequantised operands, bias. Attention is
 torch SDPA in fp32 on the CPU.
 
 Rounding points follow the B200 stack (fp16 storage between ops; the residual
-adds are fused into the linear's fp32 epilogue and rounded once), so the two
-are compared with a relative-error gate rather than bit for bit.
+adds are fused into the linear's fp32 epilogue and rounded once; GELU applies
+to the fp16 fc1 output and is rounded to fp16, as in HF), so the two are
+compared with relative-error gates rather than bit for bit.
 
 This is also the path `bench.py --impl reference` and the `cpu_baseline` leg
 time: torch-CPU fp32 dequantise + matmul on all host cores.
@@ -59,7 +60,8 @@ def encoder_layer_ref(h: torch.Tensor, qw: dict, B: int, S: int, heads: int, eps
     a = F.scaled_dot_product_attention(q, k, v).transpose(1, 2).reshape(T, D).half()
     h2 = _linear(a, qw["w_o"], qw["b_o"], residual=h, epilogue=gemm.EPI_RESIDUAL)
     x2 = norm.layernorm_ref(h2, None, qw["ln2_g"], qw["ln2_b"], eps).half()
-    f = _linear(x2, qw["w_fc1"], qw["b_fc1"], epilogue=gemm.EPI_GELU)
+    y = _linear(x2, qw["w_fc1"], qw["b_fc1"])          # fc1 output, fp16
+    f = gemm.gelu_f16(y)                                 # GELU on the fp16 output, rounded to fp16 (HF order)
     return _linear(f, qw["w_fc2"], qw["b_fc2"], residual=h2, epilogue=gemm.EPI_RESIDUAL_CLAMP)
 
 

@@ -54,6 +54,18 @@ def gemm_fp8_ref(*args, **kwargs) -> torch.Tensor:
     return gemm_fp8_ref_f32(*args, **kwargs).half()
 
 
+def gelu_f16(y16: torch.Tensor) -> torch.Tensor:
+    """fp16(gelu_erf(float(y))) for an fp16 tensor: HF's "gelu" on the fp16 fc1
+    output, rounded to fp16 (the encoder's FFN activation)."""
+    return torch.nn.functional.gelu(y16.float().cpu()).half()
+
+
+def order_key_f16(v: float) -> int:
+    """Order-preserving uint key of an fp16 value (the GEMM max-key epilogue's encoding)."""
+    h = int(np.array([v], dtype=np.float16).view(np.uint16)[0])
+    return (~h & 0xFFFF) if (h & 0x8000) else (h | 0x8000)
+
+
 def rel_error(y: torch.Tensor, ref: torch.Tensor) -> float:
     """max|y - ref| / max|ref| over the whole output (the GEMM parity metric)."""
     y = y.float().cpu()

@@ -131,3 +131,17 @@ def test_blaze_linear_fp8(cuda_device):
 
 def test_no_device_error_recorded(cuda_device):
     assert _lib.device_error() == 0
+
+
+def test_gemm_max_key_epilogue(cuda_device):
+    """'bias_maxkey': output as 'none', and out_amax receives the order key of the largest output."""
+    from oracle.gemm import order_key_f16
+    M, N, K = 300, 1000, 1280
+    aq, sa, wq, sw, b = _operands(M, N, K, 90, cuda_device)
+    key = ops.new_amax_ws(cuda_device)
+    y = ops.gemm_fp8(aq, sa, wq, sw, b, epilogue="bias_maxkey", out_amax=key)
+    y_none = ops.gemm_fp8(aq, sa, wq, sw, b)
+    assert torch.equal(y, y_none)
+    assert key.item() == order_key_f16(float(y.float().max()))
+    with pytest.raises(RuntimeError, match="requires out_amax"):
+        ops.gemm_fp8(aq, sa, wq, sw, b, epilogue="bias_maxkey")

@@ -173,3 +173,49 @@ def test_quantise_matches_live_reference_kernel(cuda_device, name, x):
         q, s = ops.quantise(xd, fmt_name)
         assert np.float32(s.item()).view(np.int32) == np.float32(s_ref).view(np.int32), (fmt_name, s.item(), s_ref)
         assert torch.equal(q.cpu(), q_ref.cpu()), f"{fmt_name}: bytes differ from the reference kernel"
+
+
+# ---- GELU + quantise of the FFN activation
+
+def _check_gelu_quant(y16, q, s):
+    """The GPU GELU uses the A&S 7.1.26 erf (|err| <= 1.5e-7), the oracle torch's exact erf: fp16 GELU
+    values may differ by one ulp, so fp8 codes may differ by one step for a small fraction of elements,
+    and the scale (from the amax of the fp16 GELU values) by one fp16 ulp of the amax."""
+    from oracle import gemm as ogemm
+    g_ref = ogemm.gelu_f16(y16).numpy()
+    s_gpu = np.float32(s.item())
+    s_ref = fp8.scale_from_amax(fp8.amax_f16(g_ref), fp8.E4M3)
+    assert abs(s_gpu / s_ref - 1.0) <= 2.0 ** -10, (s_gpu, s_ref)
+    q_ref = fp8.quantise_with_scale(g_ref, s_gpu, fp8.E4M3)
+    q = q.cpu().numpy()
+    diff = q != q_ref
+    assert diff.mean() <= 5e-3, f"{diff.mean():.4%} of fp8 codes differ"
+    a = fp8.decode(q[diff], fp8.E4M3).astype(np.float64)
+    b = fp8.decode(q_ref[diff], fp8.E4M3).astype(np.float64)
+    assert (np.abs(a - b) <= np.maximum(np.abs(a), np.abs(b)) * 2.0 ** -3 + 2.0 ** -9).all()
+
+
+@pytest.mark.parametrize("std", [0.05, 1.0, 3.0])
+def test_quantise_gelu_matches_oracle(cuda_device, std):
+    from oracle import gemm as ogemm
+    y = randn_f16((777, 1280), 300, std=std)
+    yd = y.to(cuda_device)
+    key = torch.tensor([ogemm.order_key_f16(float(y.float().max()))], dtype=torch.int32, device=cuda_device)
+    q_fast, s_fast = ops.quantise_gelu(yd, key)
+    q_full, s_full = ops.quantise_gelu(yd, None)
+    # the amax taken from max(y) is exact, so both paths agree bit for bit
+    assert torch.equal(q_fast, q_full) and s_fast.item() == s_full.item()
+    _check_gelu_quant(y, q_full, s_full)
+
+
+def test_quantise_gelu_negative_side_amax(cuda_device):
+    """All fc1 outputs <= 0.2: gelu(y_max) < 0.171 may not be the amax (negative side up to 0.17), so the
+    kernel must take the full pass even when given the max key."""
+    from oracle import gemm as ogemm
+    y = (-torch.rand(4096, generator=torch.Generator().manual_seed(5)) * 3 + 0.2).half()
+    yd = y.to(cuda_device)
+    key = torch.tensor([ogemm.order_key_f16(float(y.float().max()))], dtype=torch.int32, device=cuda_device)
+    q, s = ops.quantise_gelu(yd, key)
+    _check_gelu_quant(y, q, s)
+    g = ogemm.gelu_f16(y).float()
+    assert abs(s.item() * 448.0 - g.abs().max().item()) <= 2e-3 * g.abs().max().item()

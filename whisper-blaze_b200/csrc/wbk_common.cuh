@@ -54,6 +54,38 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
+// erf(z) for z >= 0 by Abramowitz & Stegun, Handbook of Mathematical Functions,
+// formula 7.1.26: erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^{-z^2},
+// t = 1 / (1 + p z), |error| <= 1.5e-7 — far below the fp16 resolution of a
+// GELU output — for about a third of the FMA-pipe work of erff.
+__device__ __forceinline__ float erf_nonneg_as7126(float z) {
+  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
+  float poly = fmaf(t, 1.061405429f, -1.453152027f);
+  poly = fmaf(t, poly, 1.421413741f);
+  poly = fmaf(t, poly, -0.284496736f);
+  poly = fmaf(t, poly, 0.254829592f);
+  poly *= t;
+  const float e = exp2f(-z * z * 1.4426950408889634f);  // e^{-z^2}
+  return fmaf(-poly, e, 1.0f);
+}
+
+// Exact-erf GELU (HF activation "gelu"): 0.5 v (1 + erf(v / sqrt 2)).
+__device__ __forceinline__ float gelu_erf(float v) {
+  const float z = fabsf(v) * 0.70710678118654752440f;
+  const float er = copysignf(erf_nonneg_as7126(z), v);
+  return 0.5f * v * (1.0f + er);
+}
+
+// Order-preserving key of an fp16 bit pattern, so an unsigned atomicMax finds
+// the largest (signed) value; key 0 means "no value".
+__device__ __forceinline__ uint32_t f16_order_key(uint32_t h) {
+  h &= 0xFFFFu;
+  return (h & 0x8000u) ? (~h & 0xFFFFu) : (h | 0x8000u);
+}
+__device__ __forceinline__ uint32_t f16_from_order_key(uint32_t k) {
+  return (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+}
+
 // Streaming 16-byte global load (read once, keep L1 clean).
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 r;

@@ -271,29 +271,6 @@ __device__ __forceinline__ uint64_t make_sw128_desc(const void* smem_ptr) {
 
 // ----------------------------------------------------------------- epilogue
 
-// erf(z) for z >= 0 by Abramowitz & Stegun, Handbook of Mathematical Functions,
-// formula 7.1.26: erf(z) = 1 - (a1 t + a2 t^2 + a3 t^3 + a4 t^4 + a5 t^5) e^{-z^2},
-// t = 1 / (1 + p z), |error| <= 1.5e-7 — far below the fp16 resolution of
-// the GELU output — for about a third of the FMA-pipe work of erff, which
-// matters because the epilogue runs once per output element.
-__device__ __forceinline__ float erf_nonneg_as7126(float z) {
-  const float t = __fdividef(1.0f, fmaf(0.3275911f, z, 1.0f));
-  float poly = fmaf(t, 1.061405429f, -1.453152027f);
-  poly = fmaf(t, poly, 1.421413741f);
-  poly = fmaf(t, poly, -0.284496736f);
-  poly = fmaf(t, poly, 0.254829592f);
-  poly *= t;
-  const float e = exp2f(-z * z * 1.4426950408889634f);  // e^{-z^2}
-  return fmaf(-poly, e, 1.0f);
-}
-
-// Exact-erf GELU (HF activation "gelu"): 0.5 v (1 + erf(v / sqrt 2)).
-__device__ __forceinline__ float gelu_erf(float v) {
-  const float z = fabsf(v) * 0.70710678118654752440f;
-  const float er = copysignf(erf_nonneg_as7126(z), v);
-  return 0.5f * v * (1.0f + er);
-}
-
 template <int kEpi>
 __device__ __forceinline__ float epi_apply(float v) {
   if (kEpi == WBK_EPI_GELU) v = gelu_erf(v);
@@ -311,6 +288,19 @@ __device__ __forceinline__ void add_halves8(float* v, const uint4& raw) {
 }
 
 constexpr bool has_residual(int epi) { return epi == WBK_EPI_RESIDUAL || epi == WBK_EPI_RESIDUAL_CLAMP; }
+
+// Pulls this thread's 128-column residual row segment of `tile` (256 B, two
+// 128-byte lines) into L2 ahead of use.
+template <int kEpi>
+__device__ __forceinline__ void prefetch_residual_l2(const Params& p, int tile, int quarter, int col_half, int lane) {
+  if (!has_residual(kEpi) || tile >= p.num_tiles) return;
+  const int row = (tile / p.tiles_n) * BM + quarter * 32 + lane;
+  const int col = (tile % p.tiles_n) * BN + col_half * EPI_COLS;
+  if (row >= p.M || col >= p.N) return;
+  const __half* base = p.residual + static_cast<int64_t>(row) * p.N + col;
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(base));
+  if (col + 64 < p.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + 64));
+}
 
 // Issues the residual loads of one full 32-column chunk of this thread's row
 // (4 x 16 B) so they are in flight while the previous chunk is processed.
@@ -382,6 +372,14 @@ __device__ __forceinline__ void pack_fp16(const float* v, uint32_t* w) {
     const __half2 h = __floats2half2_rn(v[2 * t], v[2 * t + 1]);
     w[t] = *reinterpret_cast<const uint32_t*>(&h);
   }
+}
+
+// Running (signed) max of v over the valid columns (fmaxf ignores NaN).
+__device__ __forceinline__ float max_valid(float m, const float* v, int valid_cols) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < valid_cols) m = fmaxf(m, v[j]);
+  return m;
 }
 
 // Running max of |v| over the valid columns (fmaxf ignores NaN). Rounding to
@@ -535,11 +533,14 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     const int quarter = warp & 3;        // TMEM lanes this warp may access: 32*quarter ..
     const int col_half = ew >> 2;        // which 128 of the 256 accumulator columns
     const float descale = p.alpha * (p.a_scale ? __ldg(p.a_scale) : 1.0f) * (p.w_scale ? __ldg(p.w_scale) : 1.0f);
-    float amax = 0.0f;
+    constexpr bool kSignedMax = (kEpi == WBK_EPI_BIAS_MAXKEY);
+    float amax = kSignedMax ? -INFINITY : 0.0f;  // max |out|, or max out for the key epilogue
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;  // staging buffer toggle (kTmaStore)
+    prefetch_residual_l2<kEpi>(p, blockIdx.x, quarter, col_half, lane);
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      prefetch_residual_l2<kEpi>(p, tile + gridDim.x, quarter, col_half, lane);  // next tile of this CTA
       const int m0 = (tile / p.tiles_n) * BM;
       const int n0 = (tile % p.tiles_n) * BN + col_half * EPI_COLS;
       const int row0 = m0 + quarter * 32;
@@ -556,7 +557,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         float v[32];
         epi_values<kEpi, kTmaStore>(p, regs, res, row, col0, descale, v);
         const int valid_cols = (row < p.M) ? min(CHUNK, p.N - col0) : 0;
-        amax = absmax_valid(amax, v, valid_cols);
+        amax = kSignedMax ? max_valid(amax, v, valid_cols) : absmax_valid(amax, v, valid_cols);
         uint32_t w[16];
         pack_fp16(v, w);
         if (kTmaStore) {
@@ -628,7 +629,8 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     }
     if (kTmaStore && lane == 0) bulk_wait_all();  // all of this warp's stores have landed
     if (p.out_amax != nullptr) {
-      const uint32_t bits = warp_max_u32(__half_as_ushort(__float2half_rn(amax)));
+      const uint32_t h = __half_as_ushort(__float2half_rn(amax));
+      const uint32_t bits = warp_max_u32(kSignedMax ? f16_order_key(h) : h);
       if (lane == 0 && bits != 0u) atomicMax(p.out_amax, bits);
     }
   }
@@ -741,10 +743,12 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, 
   if (K % 16 != 0) return fail(WBK_ERR_UNSUPPORTED, "wbk_gemm_fp8: K=%lld must be a multiple of 16 (TMA row pitch)", (long long)K);
   if ((a_fmt != WBK_FMT_E4M3 && a_fmt != WBK_FMT_E5M2) || (w_fmt != WBK_FMT_E4M3 && w_fmt != WBK_FMT_E5M2))
     return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: unknown fp8 format");
-  if (epilogue < WBK_EPI_NONE || epilogue > WBK_EPI_RESIDUAL_CLAMP)
+  if (epilogue < WBK_EPI_NONE || epilogue > WBK_EPI_BIAS_MAXKEY)
     return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: unknown epilogue %d", epilogue);
   const bool needs_res = epilogue == WBK_EPI_RESIDUAL || epilogue == WBK_EPI_RESIDUAL_CLAMP;
   if (needs_res && residual == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: residual epilogue without residual");
+  if (epilogue == WBK_EPI_BIAS_MAXKEY && out_amax_bits == nullptr)
+    return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: the max-key epilogue needs out_amax_bits");
   if (M == 0) return WBK_OK;
   if (A == nullptr || W == nullptr || out == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: null pointer");
   if (!aligned(A, 16) || !aligned(W, 16)) return fail(WBK_ERR_UNSUPPORTED, "wbk_gemm_fp8: A and W must be 16-byte aligned");
@@ -795,7 +799,8 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, 
     case WBK_EPI_NONE: return dispatch_store<WBK_EPI_NONE>(vec, ta, tw, to, p, grid, s);
     case WBK_EPI_GELU: return dispatch_store<WBK_EPI_GELU>(vec, ta, tw, to, p, grid, s);
     case WBK_EPI_RESIDUAL: return dispatch_store<WBK_EPI_RESIDUAL>(vec, ta, tw, to, p, grid, s);
-    default: return dispatch_store<WBK_EPI_RESIDUAL_CLAMP>(vec, ta, tw, to, p, grid, s);
+    case WBK_EPI_RESIDUAL_CLAMP: return dispatch_store<WBK_EPI_RESIDUAL_CLAMP>(vec, ta, tw, to, p, grid, s);
+    default: return dispatch_store<WBK_EPI_BIAS_MAXKEY>(vec, ta, tw, to, p, grid, s);
   }
 }
 

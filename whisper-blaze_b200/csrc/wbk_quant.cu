@@ -139,6 +139,106 @@ quantise_f16_kernel(const __half* __restrict__ x, int64_t n, const uint32_t* __r
   }
 }
 
+// ------------------------------------------------------- GELU + quantise
+//
+// The FFN activation of the encoder is quantised right after the GELU. Here
+// the GELU runs inside the quantiser pass (this pass reads the fc1 output
+// anyway), on the fp16 fc1 output, rounded to fp16 like the stored GELU
+// output of the reference path: g = fp16(gelu(float(y))).
+//
+// The per-tensor amax of g normally needs its own pass over y. It does not
+// here: GELU is increasing for y >= -0.7518 and |gelu(y)| <= 0.16997 below
+// that, and rounding to fp16 is monotone, so when g(y_max) >= 0.171 the amax of
+// g is exactly g(y_max), where y_max is the largest fc1 output — which the
+// GEMM epilogue already tracks (WBK_EPI_BIAS_MAXKEY). Otherwise a full pass
+// computes max |g| element by element.
+
+constexpr float kGeluNegativeMaxAbs = 0.171f;  // > max over y < 0 of |fp16(gelu(y))| (0.1700)
+
+__device__ __forceinline__ uint32_t gelu_f16_bits(uint32_t h) {
+  return __half_as_ushort(__float2half_rn(gelu_erf(half_bits_to_float(h))));
+}
+
+template <bool kVec>
+__global__ void __launch_bounds__(kThreads)
+gelu_amax_kernel(const __half* __restrict__ y, int64_t n, const uint32_t* __restrict__ ymax_key,
+                 uint32_t* __restrict__ amax_bits) {
+  if (ymax_key != nullptr) {
+    const uint32_t key = *ymax_key;
+    if (key != 0u) {
+      const uint32_t g = gelu_f16_bits(f16_from_order_key(key));
+      const float gf = half_bits_to_float(g);
+      if (gf >= kGeluNegativeMaxAbs) {  // false for NaN
+        if (blockIdx.x == 0 && threadIdx.x == 0) atomicMax(amax_bits, g & 0x7FFFu);
+        return;  // uniform across the grid: every CTA reads the same key
+      }
+    }
+  }
+  uint32_t m = 0;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (kVec) {
+    const int64_t nvec = n >> 3;
+    const uint4* yv = reinterpret_cast<const uint4*>(y);
+    for (int64_t i = tid; i < nvec; i += stride) {
+      const uint4 v = ld_stream16(yv + i);
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t g = gelu_f16_bits(w[k]) | (gelu_f16_bits(w[k] >> 16) << 16);
+        m = __vmaxu2(m, abs2_nonan(g));
+      }
+    }
+    done = nvec << 3;
+  }
+  const unsigned short* ys = reinterpret_cast<const unsigned short*>(y);
+  for (int64_t i = done + tid; i < n; i += stride) m = __vmaxu2(m, abs2_nonan(gelu_f16_bits(ys[i])));
+  uint32_t mm = warp_max_u32(max(m & 0xFFFFu, m >> 16));
+  __shared__ uint32_t red[kThreads / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) red[warp] = mm;
+  __syncthreads();
+  if (warp == 0) {
+    mm = warp_max_u32(lane < kThreads / 32 ? red[lane] : 0u);
+    if (lane == 0 && mm != 0u) atomicMax(amax_bits, mm);
+  }
+}
+
+template <int kFmt>
+__device__ __forceinline__ uint32_t gelu_q8x4(uint32_t h01, uint32_t h23, float inv, float mx) {
+  const uint32_t g01 = gelu_f16_bits(h01) | (gelu_f16_bits(h01 >> 16) << 16);
+  const uint32_t g23 = gelu_f16_bits(h23) | (gelu_f16_bits(h23 >> 16) << 16);
+  return q8x4<kFmt>(g01, g23, inv, mx);
+}
+
+template <int kFmt, bool kVec>
+__global__ void __launch_bounds__(kThreads)
+quantise_gelu_kernel(const __half* __restrict__ y, int64_t n, const uint32_t* __restrict__ amax_bits,
+                     float max_fp8, uint8_t* __restrict__ q, float* __restrict__ scale_out) {
+  float scale, inv;
+  scale_from_amax(*amax_bits, max_fp8, scale, inv);
+  if (scale_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (kVec) {
+    const int64_t nvec = n >> 3;
+    const uint4* yv = reinterpret_cast<const uint4*>(y);
+    uint2* qv = reinterpret_cast<uint2*>(q);
+    for (int64_t i = tid; i < nvec; i += stride) {
+      const uint4 v = ld_stream16(yv + i);
+      qv[i] = make_uint2(gelu_q8x4<kFmt>(v.x, v.y, inv, max_fp8), gelu_q8x4<kFmt>(v.z, v.w, inv, max_fp8));
+    }
+    done = nvec << 3;
+  }
+  const unsigned short* ys = reinterpret_cast<const unsigned short*>(y);
+  for (int64_t i = done + tid; i < n; i += stride) {
+    const float g = half_bits_to_float(gelu_f16_bits(ys[i]));
+    q[i] = static_cast<uint8_t>(q8x2<kFmt>(g, 0.0f, inv, max_fp8) & 0xFFu);
+  }
+}
+
 // -------------------------------------------------------------- dequantise
 
 template <int kFmt>
@@ -325,6 +425,33 @@ int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out, float* scal
   if (int e = cuda_check(cudaMemsetAsync(amax_ws, 0, sizeof(uint32_t), s), "wbk_quantise_f16 memset")) return e;
   if (int e = wbk_amax_f16(x, n, amax_ws, stream)) return e;
   return wbk_quantise_from_amax_f16(x, n, fmt, amax_ws, q_out, scale_out, stream);
+}
+
+int wbk_quantise_gelu_f16(const void* y, int64_t n, int fmt, const uint32_t* ymax_key, void* q_out,
+                          float* scale_out, uint32_t* amax_ws, wbk_stream_t stream) {
+  if (int e = check_fmt(fmt)) return e;
+  if (amax_ws == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_gelu_f16: amax_ws is null");
+  if (n < 0) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_gelu_f16: n < 0");
+  if (n > 0 && (y == nullptr || q_out == nullptr)) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_gelu_f16: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const __half* yh = static_cast<const __half*>(y);
+  if (int e = cuda_check(cudaMemsetAsync(amax_ws, 0, sizeof(uint32_t), s), "wbk_quantise_gelu_f16 memset")) return e;
+  const bool vec = aligned(y, 16) && aligned(q_out, 8);
+  const int agrid = grid_for(vec ? (n + 7) / 8 : n, 8);
+  if (vec) gelu_amax_kernel<true><<<agrid, kThreads, 0, s>>>(yh, n, ymax_key, amax_ws);
+  else gelu_amax_kernel<false><<<agrid, kThreads, 0, s>>>(yh, n, ymax_key, amax_ws);
+  if (int e = cuda_check(cudaGetLastError(), "wbk_quantise_gelu_f16 amax launch")) return e;
+  const int grid = grid_for(vec ? (n + 7) / 8 : n, 16);
+  const float mx = fmt_max(fmt);
+  uint8_t* q = static_cast<uint8_t*>(q_out);
+  if (fmt == WBK_FMT_E4M3) {
+    if (vec) quantise_gelu_kernel<WBK_FMT_E4M3, true><<<grid, kThreads, 0, s>>>(yh, n, amax_ws, mx, q, scale_out);
+    else quantise_gelu_kernel<WBK_FMT_E4M3, false><<<grid, kThreads, 0, s>>>(yh, n, amax_ws, mx, q, scale_out);
+  } else {
+    if (vec) quantise_gelu_kernel<WBK_FMT_E5M2, true><<<grid, kThreads, 0, s>>>(yh, n, amax_ws, mx, q, scale_out);
+    else quantise_gelu_kernel<WBK_FMT_E5M2, false><<<grid, kThreads, 0, s>>>(yh, n, amax_ws, mx, q, scale_out);
+  }
+  return cuda_check(cudaGetLastError(), "wbk_quantise_gelu_f16 launch");
 }
 
 int wbk_dequantise_f16(const void* q, int64_t n, int fmt, float scale, void* out, wbk_stream_t stream) {

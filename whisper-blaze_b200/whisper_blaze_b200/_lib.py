@@ -29,6 +29,7 @@ EPI_NONE = 0
 EPI_GELU = 1
 EPI_RESIDUAL = 2
 EPI_RESIDUAL_CLAMP = 3
+EPI_BIAS_MAXKEY = 4
 
 _vp, _i64, _i32, _u64, _f32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_uint64, ctypes.c_float
 
@@ -42,6 +43,7 @@ _PROTOTYPES = {
     "wbk_quantise_from_amax_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "wbk_quantise_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "wbk_quantise_f16_noalloc": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp]),
+    "wbk_quantise_gelu_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp, _vp]),
     "wbk_dequantise_f16": (_i32, [_vp, _i64, _i32, _f32, _vp, _vp]),
     "wbk_layernorm_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp]),
     "wbk_rmsnorm_f16": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),

@@ -16,8 +16,8 @@ Per layer, on one stream and without any host synchronisation:
   out-proj GEMM     -> h2 = fp16(acc*s + b + h)        residual epilogue
   LN2(h2)           -> x2  + amax(x2)                  norm kernel
   quantise(x2)      -> x2q                             quantise kernel
-  fc1 GEMM          -> f = fp16(gelu(acc*s + b)) + amax(f)   GELU epilogue
-  quantise(f)       -> fq
+  fc1 GEMM          -> y = fp16(acc*s + b) + max(y)          bias + max-key epilogue
+  gelu+quantise(y)  -> fq = q8(fp16(gelu(y)))              (amax of the GELU output from max(y))
   fc2 GEMM          -> h' = fp16(clamp(acc*s + b + h2))      residual+clamp epilogue
 
 Activation scales live in device memory; weights are quantised once.
@@ -162,7 +162,7 @@ class FP8EncoderStack:
         self.f = e(T, Fd)
         self.fq = e(T, Fd, dt=torch.uint8)
         self.out = e(T, D)
-        self.amax = torch.zeros(4, dtype=torch.int32, device=dev)
+        self.amax = torch.zeros(8, dtype=torch.int32, device=dev)
         self.scales = torch.ones(4, dtype=torch.float32, device=dev)
         self._ws_tokens = T
 
@@ -211,9 +211,9 @@ class FP8EncoderStack:
         ops.layernorm(self.h2, None, L.ln2_g, L.ln2_b, cfg.eps, out=self.x, out_amax=amax[2:3])
         ops.quantise_from_amax(self.x, amax[2:3], q_out=self.xq, scale_out=sc[2:3])
         keep("ln2", self.x), keep("ln2_q", self.xq), keep("ln2_s", sc[2:3])
-        self._gemm("fc1", 2 * T * D * Fd, self.xq, sc[2:3], L.w_fc1, L.s_fc1, L.b_fc1, epilogue="gelu",
+        self._gemm("fc1", 2 * T * D * Fd, self.xq, sc[2:3], L.w_fc1, L.s_fc1, L.b_fc1, epilogue="bias_maxkey",
                    out=self.f, out_amax=amax[3:4])
-        ops.quantise_from_amax(self.f, amax[3:4], q_out=self.fq, scale_out=sc[3:4])
+        ops.quantise_gelu(self.f, amax[3:4], q_out=self.fq, scale_out=sc[3:4], amax_ws=amax[4:5])
         keep("fc1", self.f), keep("fc1_q", self.fq), keep("fc1_s", sc[3:4])
         self._gemm("fc2", 2 * T * Fd * D, self.fq, sc[3:4], L.w_fc2, L.s_fc2, L.b_fc2, residual=self.h2,
                    epilogue="residual_clamp", out=h_next)

@@ -12,8 +12,8 @@ from typing import Optional, Sequence, Union
 import torch
 
 from . import _lib
-from ._lib import (EPI_GELU, EPI_NONE, EPI_RESIDUAL, EPI_RESIDUAL_CLAMP, FMT_E4M3, FMT_E5M2, check, lib, ptr,
-                   stream_of)
+from ._lib import (EPI_BIAS_MAXKEY, EPI_GELU, EPI_NONE, EPI_RESIDUAL, EPI_RESIDUAL_CLAMP, FMT_E4M3, FMT_E5M2,
+                   check, lib, ptr, stream_of)
 
 Scale = Union[float, torch.Tensor]
 
@@ -28,8 +28,9 @@ def _count(n: int = 1) -> None:
 
 _FMT_BY_NAME = {"e4m3": FMT_E4M3, "e5m2": FMT_E5M2, FMT_E4M3: FMT_E4M3, FMT_E5M2: FMT_E5M2}
 _EPI_BY_NAME = {"none": EPI_NONE, "bias": EPI_NONE, "gelu": EPI_GELU, "residual": EPI_RESIDUAL,
-                "residual_clamp": EPI_RESIDUAL_CLAMP, EPI_NONE: EPI_NONE, EPI_GELU: EPI_GELU,
-                EPI_RESIDUAL: EPI_RESIDUAL, EPI_RESIDUAL_CLAMP: EPI_RESIDUAL_CLAMP}
+                "residual_clamp": EPI_RESIDUAL_CLAMP, "bias_maxkey": EPI_BIAS_MAXKEY, EPI_NONE: EPI_NONE,
+                EPI_GELU: EPI_GELU, EPI_RESIDUAL: EPI_RESIDUAL, EPI_RESIDUAL_CLAMP: EPI_RESIDUAL_CLAMP,
+                EPI_BIAS_MAXKEY: EPI_BIAS_MAXKEY}
 _BYTE_DTYPES = {torch.uint8, torch.int8, torch.float8_e4m3fn, torch.float8_e5m2}
 
 
@@ -118,6 +119,27 @@ def quantise(x: torch.Tensor, fmt="e4m3", q_out: Optional[torch.Tensor] = None,
     with torch.cuda.device(x.device):
         check(lib().wbk_quantise_f16(x.data_ptr(), x.numel(), f, q.data_ptr(), s.data_ptr(), ws.data_ptr(),
                                      stream_of(x)), "quantise")
+    _count(2)
+    return q, s
+
+
+def quantise_gelu(y: torch.Tensor, ymax_key: Optional[torch.Tensor] = None, fmt="e4m3",
+                  q_out: Optional[torch.Tensor] = None, scale_out: Optional[torch.Tensor] = None,
+                  amax_ws: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Quantise fp16(gelu(y)) per tensor without storing the GELU output.
+
+    ymax_key: the max-key word written by a GEMM with the 'bias_maxkey'
+    epilogue over y (lets the amax come from y's maximum), or None."""
+    require_input(y, "y")
+    require_fp16(y, "y")
+    f = fmt_code(fmt)
+    q = torch.empty(y.shape, dtype=torch.uint8, device=y.device) if q_out is None else q_out
+    s = torch.empty(1, dtype=torch.float32, device=y.device) if scale_out is None else scale_out
+    ws = torch.empty(1, dtype=torch.int32, device=y.device) if amax_ws is None else amax_ws
+    require_same_device(y, ymax_key, q, s, ws)
+    with torch.cuda.device(y.device):
+        check(lib().wbk_quantise_gelu_f16(y.data_ptr(), y.numel(), f, ptr(ymax_key), q.data_ptr(), s.data_ptr(),
+                                          ws.data_ptr(), stream_of(y)), "quantise_gelu")
     _count(2)
     return q, s
 
@@ -211,7 +233,8 @@ def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
 
     a: fp8 codes [..., K]; w: fp8 codes [N, K] (nn.Linear layout); scales as
     Python floats or 1-element fp32 CUDA tensors; epilogue one of
-    'none' | 'gelu' | 'residual' | 'residual_clamp'.
+    'none' | 'gelu' | 'residual' | 'residual_clamp' | 'bias_maxkey' (bias only, and
+    out_amax receives the order key of the largest output, for quantise_gelu).
     """
     require_input(a, "a_fp8")
     require_input(w, "w_fp8")
@@ -239,6 +262,8 @@ def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
             raise RuntimeError(f"residual must have shape {out_shape}")
     if epi in (EPI_RESIDUAL, EPI_RESIDUAL_CLAMP) and residual is None:
         raise RuntimeError("residual epilogue requires a residual tensor")
+    if epi == EPI_BIAS_MAXKEY and out_amax is None:
+        raise RuntimeError("the bias_maxkey epilogue requires out_amax")
     alpha_a, pa = _scale_arg(a_scale, "a_scale", a.device)
     alpha_w, pw = _scale_arg(w_scale, "w_scale", a.device)
     alpha = float(torch.tensor(alpha_a, dtype=torch.float32) * torch.tensor(alpha_w, dtype=torch.float32))
