@@ -212,13 +212,34 @@ __device__ __forceinline__ uint32_t gelu_q8x4(uint32_t h01, uint32_t h23, float 
   return q8x4<kFmt>(g01, g23, inv, mx);
 }
 
+// The GELU output g = fp16(gelu(float(y))) depends only on the 16 bits of y,
+// so each CTA first evaluates it once for all 65536 fp16 bit patterns into a
+// 128 KB shared-memory table (with the same device function, so the result is
+// bit-identical to evaluating it per element) and then needs one table lookup
+// per element: the pass becomes HBM-bound instead of FMA-bound.
+constexpr int kGeluThreads = 1024;
+constexpr size_t kGeluTableBytes = 65536 * sizeof(uint16_t);
+
+__device__ __forceinline__ uint32_t gelu_lookup2(const uint16_t* table, uint32_t h2) {
+  return static_cast<uint32_t>(table[h2 & 0xFFFFu]) | (static_cast<uint32_t>(table[h2 >> 16]) << 16);
+}
+
+template <int kFmt>
+__device__ __forceinline__ uint2 gelu_q8x8(const uint16_t* table, const uint4& v, float inv, float mx) {
+  return make_uint2(q8x4<kFmt>(gelu_lookup2(table, v.x), gelu_lookup2(table, v.y), inv, mx),
+                    q8x4<kFmt>(gelu_lookup2(table, v.z), gelu_lookup2(table, v.w), inv, mx));
+}
+
 template <int kFmt, bool kVec>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kGeluThreads, 1)
 quantise_gelu_kernel(const __half* __restrict__ y, int64_t n, const uint32_t* __restrict__ amax_bits,
                      float max_fp8, uint8_t* __restrict__ q, float* __restrict__ scale_out) {
+  extern __shared__ uint16_t gelu_table[];
+  for (uint32_t h = threadIdx.x; h < 65536u; h += kGeluThreads) gelu_table[h] = static_cast<uint16_t>(gelu_f16_bits(h));
   float scale, inv;
   scale_from_amax(*amax_bits, max_fp8, scale, inv);
   if (scale_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+  __syncthreads();
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   int64_t done = 0;
@@ -226,17 +247,51 @@ quantise_gelu_kernel(const __half* __restrict__ y, int64_t n, const uint32_t* __
     const int64_t nvec = n >> 3;
     const uint4* yv = reinterpret_cast<const uint4*>(y);
     uint2* qv = reinterpret_cast<uint2*>(q);
-    for (int64_t i = tid; i < nvec; i += stride) {
-      const uint4 v = ld_stream16(yv + i);
-      qv[i] = make_uint2(gelu_q8x4<kFmt>(v.x, v.y, inv, max_fp8), gelu_q8x4<kFmt>(v.z, v.w, inv, max_fp8));
+    int64_t i = tid;
+    for (; i + 3 * stride < nvec; i += 4 * stride) {
+      const uint4 v0 = ld_stream16(yv + i);
+      const uint4 v1 = ld_stream16(yv + i + stride);
+      const uint4 v2 = ld_stream16(yv + i + 2 * stride);
+      const uint4 v3 = ld_stream16(yv + i + 3 * stride);
+      qv[i] = gelu_q8x8<kFmt>(gelu_table, v0, inv, max_fp8);
+      qv[i + stride] = gelu_q8x8<kFmt>(gelu_table, v1, inv, max_fp8);
+      qv[i + 2 * stride] = gelu_q8x8<kFmt>(gelu_table, v2, inv, max_fp8);
+      qv[i + 3 * stride] = gelu_q8x8<kFmt>(gelu_table, v3, inv, max_fp8);
     }
+    for (; i < nvec; i += stride) qv[i] = gelu_q8x8<kFmt>(gelu_table, ld_stream16(yv + i), inv, max_fp8);
     done = nvec << 3;
   }
   const unsigned short* ys = reinterpret_cast<const unsigned short*>(y);
   for (int64_t i = done + tid; i < n; i += stride) {
-    const float g = half_bits_to_float(gelu_f16_bits(ys[i]));
+    const float g = half_bits_to_float(gelu_table[ys[i]]);
     q[i] = static_cast<uint8_t>(q8x2<kFmt>(g, 0.0f, inv, max_fp8) & 0xFFu);
   }
+}
+
+template <int kFmt, bool kVec>
+int launch_quantise_gelu(const __half* y, int64_t n, const uint32_t* amax, float mx, uint8_t* q, float* scale_out,
+                         cudaStream_t s) {
+  static std::mutex mu;
+  static std::vector<char> configured;
+  const int dev = current_device();
+  if (dev < 0) return fail(WBK_ERR_CUDA, "wbk_quantise_gelu_f16: no current CUDA device");
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
+    if (!configured[dev]) {
+      if (int e = cuda_check(cudaFuncSetAttribute(quantise_gelu_kernel<kFmt, kVec>,
+                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(kGeluTableBytes)),
+                             "wbk_quantise_gelu_f16: cudaFuncSetAttribute"))
+        return e;
+      configured[dev] = 1;
+    }
+  }
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t want = ((kVec ? (n + 7) / 8 : n) + kGeluThreads - 1) / kGeluThreads;
+  const int grid = static_cast<int>(want < 1 ? 1 : (want < sms ? want : sms));
+  quantise_gelu_kernel<kFmt, kVec><<<grid, kGeluThreads, kGeluTableBytes, s>>>(y, n, amax, mx, q, scale_out);
+  return cuda_check(cudaGetLastError(), "wbk_quantise_gelu_f16 launch");
 }
 
 // -------------------------------------------------------------- dequantise
@@ -441,17 +496,13 @@ int wbk_quantise_gelu_f16(const void* y, int64_t n, int fmt, const uint32_t* yma
   if (vec) gelu_amax_kernel<true><<<agrid, kThreads, 0, s>>>(yh, n, ymax_key, amax_ws);
   else gelu_amax_kernel<false><<<agrid, kThreads, 0, s>>>(yh, n, ymax_key, amax_ws);
   if (int e = cuda_check(cudaGetLastError(), "wbk_quantise_gelu_f16 amax launch")) return e;
-  const int grid = grid_for(vec ? (n + 7) / 8 : n, 16);
   const float mx = fmt_max(fmt);
   uint8_t* q = static_cast<uint8_t*>(q_out);
-  if (fmt == WBK_FMT_E4M3) {
-    if (vec) quantise_gelu_kernel<WBK_FMT_E4M3, true><<<grid, kThreads, 0, s>>>(yh, n, amax_ws, mx, q, scale_out);
-    else quantise_gelu_kernel<WBK_FMT_E4M3, false><<<grid, kThreads, 0, s>>>(yh, n, amax_ws, mx, q, scale_out);
-  } else {
-    if (vec) quantise_gelu_kernel<WBK_FMT_E5M2, true><<<grid, kThreads, 0, s>>>(yh, n, amax_ws, mx, q, scale_out);
-    else quantise_gelu_kernel<WBK_FMT_E5M2, false><<<grid, kThreads, 0, s>>>(yh, n, amax_ws, mx, q, scale_out);
-  }
-  return cuda_check(cudaGetLastError(), "wbk_quantise_gelu_f16 launch");
+  if (fmt == WBK_FMT_E4M3)
+    return vec ? launch_quantise_gelu<WBK_FMT_E4M3, true>(yh, n, amax_ws, mx, q, scale_out, s)
+               : launch_quantise_gelu<WBK_FMT_E4M3, false>(yh, n, amax_ws, mx, q, scale_out, s);
+  return vec ? launch_quantise_gelu<WBK_FMT_E5M2, true>(yh, n, amax_ws, mx, q, scale_out, s)
+             : launch_quantise_gelu<WBK_FMT_E5M2, false>(yh, n, amax_ws, mx, q, scale_out, s);
 }
 
 int wbk_dequantise_f16(const void* q, int64_t n, int fmt, float scale, void* out, wbk_stream_t stream) {
