@@ -117,6 +117,12 @@ int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out,
 int wbk_quantise_f16_noalloc(const void* x, int64_t n, int fmt, void* q_out,
                              float* scale_out, wbk_stream_t stream);
 
+/* scale_inv[0] = scale, scale_inv[1] = 1/scale for an accumulated amax, by the
+ * same rule (and the same compiled division) as wbk_quantise_from_amax_f16.
+ * Used by fused producers that quantise their own output. */
+int wbk_scale_from_amax(const uint32_t* amax_bits, int fmt, float* scale_inv,
+                        wbk_stream_t stream);
+
 /* FFN activation quantiser: g = fp16(gelu_erf(float(y))) for n fp16 values y
  * (the fc1 output), then the per-tensor quantise of g exactly as
  * wbk_quantise_f16 does it (scale from max|g|). g itself is not stored.
@@ -152,6 +158,23 @@ int wbk_layernorm_f16(const void* x, const void* residual, const void* gamma,
                       const void* beta, void* out, void* sum_out,
                       int64_t rows, int64_t D, float eps,
                       uint32_t* out_amax_bits, wbk_stream_t stream);
+
+/* LayerNorm followed by the per-tensor FP8 quantise of its output, without
+ * storing the fp16 output: pass 1 writes each row's mean and rstd to `ws` and
+ * the amax of the fp16 LayerNorm outputs to *amax_ws; pass 2 recomputes the
+ * same fp16 outputs from x and the stored statistics and writes only their
+ * fp8 codes. Bit-identical to wbk_layernorm_f16 (residual NULL) followed by
+ * wbk_quantise_f16, with 2 fewer bytes of HBM traffic per element.
+ * D % 8 == 0 and D <= 4096. ws: caller-owned device buffer of
+ * wbk_layernorm_quantise_ws_bytes(rows) bytes; amax_ws: a device uint32.
+ * Replaces: layernorm_fused (csrc/kernels/layernorm_fused.cu:50-184) followed
+ * by quantise_to_e4m3 (csrc/kernels/fp8_quantize.cu:222-238), as the FP8 linear
+ * after a pre-LN (whisper_blaze/model.py:93-96) would run them. */
+int wbk_layernorm_quantise_f16(const void* x, const void* gamma, const void* beta,
+                               int64_t rows, int64_t D, float eps, int fmt,
+                               void* q_out, float* scale_out, void* ws,
+                               uint32_t* amax_ws, wbk_stream_t stream);
+int64_t wbk_layernorm_quantise_ws_bytes(int64_t rows);
 
 /* out = fp16((x + residual) * rsqrt(mean((x+residual)^2) + eps) * gamma),
  * residual required, D % 8 == 0.

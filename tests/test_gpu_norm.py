@@ -113,3 +113,16 @@ def test_layernorm_matches_live_reference_kernel(cuda_device):
     r_ref = R.rmsnorm_fused(x, res, g, 1e-5)
     r = ops.rmsnorm(x, res, g, 1e-5)
     assert ((r.float() - r_ref.float()).abs() <= norm.ln_tolerance(r_ref.float().cpu()).to(cuda_device)).all()
+
+
+@pytest.mark.parametrize("rows,D", [(1, 8), (7, 64), (1500, 1280), (333, 1288), (64, 4096)])
+@pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
+def test_layernorm_quantise_is_bit_identical_to_unfused(cuda_device, rows, D, fmt):
+    """The fused LayerNorm->FP8 path writes exactly the codes and scale of LayerNorm then quantise."""
+    x = randn_f16((rows, D), 70 + rows).to(cuda_device) * 3
+    g, b = (t.to(cuda_device) for t in _params(D, 71))
+    ln, _ = ops.layernorm(x, None, g, b)
+    q_ref, s_ref = ops.quantise(ln, fmt)
+    q, s = ops.layernorm_quantise(x, g, b, fmt=fmt)
+    assert s.view(torch.int32).item() == s_ref.view(torch.int32).item()
+    assert torch.equal(q, q_ref)

@@ -59,85 +59,145 @@ __device__ __forceinline__ void block_amax_commit(uint32_t m, uint32_t* out_amax
   }
 }
 
-// kVpl = 16-byte vectors (8 halves) per lane; the row has D/8 vectors.
+// Per-row pieces shared by every mode of norm_warp_kernel, so the stats-only
+// pass and the quantise pass of the fused LayerNorm->FP8 path compute exactly
+// the same fp16 outputs as the plain LayerNorm.
+template <int kVpl>
+__device__ __forceinline__ void load_row(const uint4* xr, const uint4* rr, int lane, int nvec, float (&v)[kVpl][8]) {
+#pragma unroll
+  for (int i = 0; i < kVpl; ++i) {
+    const int idx = lane + 32 * i;
+    if (idx < nvec) {
+      unpack8(ld_stream16(xr + idx), v[i]);
+      if (rr) {
+        float r8[8];
+        unpack8(ld_stream16(rr + idx), r8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += r8[j];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+    }
+  }
+}
+
 template <int kVpl, bool kRms>
+__device__ __forceinline__ void row_stats(const float (&v)[kVpl][8], int lane, int nvec, float fD, float eps,
+                                          float& mean, float& inv) {
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kVpl; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += kRms ? v[i][j] * v[i][j] : v[i][j];
+  s = warp_sum(s);
+  if (kRms) {
+    mean = 0.0f;
+    inv = rsqrtf(s / fD + eps);
+    return;
+  }
+  mean = s / fD;
+  float var = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kVpl; ++i) {
+    if (lane + 32 * i < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = v[i][j] - mean;
+        var += d * d;
+      }
+    }
+  }
+  var = warp_sum(var);
+  inv = rsqrtf(var / fD + eps);
+}
+
+template <bool kRms>
+__device__ __forceinline__ uint4 normalise8(const float* v8, int idx, const __half* __restrict__ gamma,
+                                            const __half* __restrict__ beta, float mean, float inv) {
+  float g[8], o[8];
+  unpack8(__ldg(reinterpret_cast<const uint4*>(gamma) + idx), g);
+  if (kRms) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = (v8[j] * inv) * g[j];
+  } else {
+    float b[8];
+    unpack8(__ldg(reinterpret_cast<const uint4*>(beta) + idx), b);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = fmaf((v8[j] - mean) * inv, g[j], b[j]);
+  }
+  return pack8(o);
+}
+
+enum NormMode { kModeNormal = 0, kModeStats = 1, kModeQuant = 2 };
+
+// kVpl = 16-byte vectors (8 halves) per lane; the row has D/8 vectors.
+//   kModeNormal: out (+ sum_out, + out_amax) as wbk_layernorm_f16 / wbk_rmsnorm_f16;
+//   kModeStats:  stats[row] = (mean, rstd) and out_amax of the fp16 outputs, nothing else stored;
+//   kModeQuant:  fp8 codes of the fp16 outputs, from stats[] and scale_inv = (scale, 1/scale).
+template <int kVpl, bool kRms, int kMode, int kFmt>
 __global__ void __launch_bounds__(kThreads)
 norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, const __half* __restrict__ gamma,
                  const __half* __restrict__ beta, __half* __restrict__ out, __half* __restrict__ sum_out,
-                 int64_t rows, int D, float eps, uint32_t* __restrict__ out_amax) {
+                 int64_t rows, int D, float eps, uint32_t* __restrict__ out_amax, float2* __restrict__ stats,
+                 const float* __restrict__ scale_inv, uint8_t* __restrict__ q_out, float* __restrict__ scale_out) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = D >> 3;
   const float fD = static_cast<float>(D);
   uint32_t amax = 0;
+  float qinv = 0.0f;
+  constexpr float kMx = kFmt == WBK_FMT_E4M3 ? 448.0f : 57344.0f;
+  if (kMode == kModeQuant) {
+    qinv = scale_inv[1];
+    if (scale_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale_inv[0];
+  }
   for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp; row < rows;
        row += static_cast<int64_t>(gridDim.x) * kWarps) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + row * D);
     const uint4* rr = res ? reinterpret_cast<const uint4*>(res + row * D) : nullptr;
     float v[kVpl][8];
-    float s = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kVpl; ++i) {
-      const int idx = lane + 32 * i;
-      if (idx < nvec) {
-        unpack8(ld_stream16(xr + idx), v[i]);
-        if (rr) {
-          float r8[8];
-          unpack8(ld_stream16(rr + idx), r8);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) v[i][j] += r8[j];
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) s += kRms ? v[i][j] * v[i][j] : v[i][j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
-      }
-    }
-    s = warp_sum(s);
-    float mean = 0.0f, inv;
-    if (kRms) {
-      inv = rsqrtf(s / fD + eps);
+    load_row<kVpl>(xr, rr, lane, nvec, v);
+    float mean, inv;
+    if (kMode == kModeQuant) {
+      const float2 st = stats[row];
+      mean = st.x;
+      inv = st.y;
     } else {
-      mean = s / fD;
-      float var = 0.0f;
-#pragma unroll
-      for (int i = 0; i < kVpl; ++i) {
-        if (lane + 32 * i < nvec) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const float d = v[i][j] - mean;
-            var += d * d;
-          }
-        }
-      }
-      var = warp_sum(var);
-      inv = rsqrtf(var / fD + eps);
+      row_stats<kVpl, kRms>(v, lane, nvec, fD, eps, mean, inv);
+      if (kMode == kModeStats && lane == 0) stats[row] = make_float2(mean, inv);
     }
-    uint4* orow = reinterpret_cast<uint4*>(out + row * D);
-    uint4* srow = sum_out ? reinterpret_cast<uint4*>(sum_out + row * D) : nullptr;
 #pragma unroll
     for (int i = 0; i < kVpl; ++i) {
       const int idx = lane + 32 * i;
       if (idx < nvec) {
-        float g[8], o[8];
-        unpack8(__ldg(reinterpret_cast<const uint4*>(gamma) + idx), g);
-        if (kRms) {
-#pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = (v[i][j] * inv) * g[j];
-        } else {
-          float b[8];
-          unpack8(__ldg(reinterpret_cast<const uint4*>(beta) + idx), b);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = ((v[i][j] - mean) * inv) * g[j] + b[j];
+        const uint4 ov = normalise8<kRms>(v[i], idx, gamma, beta, mean, inv);
+        if (kMode == kModeNormal) {
+          reinterpret_cast<uint4*>(out + row * D)[idx] = ov;
+          if (sum_out) reinterpret_cast<uint4*>(sum_out + row * D)[idx] = pack8(v[i]);
         }
-        const uint4 ov = pack8(o);
-        orow[idx] = ov;
-        if (out_amax) amax = max(amax, amax8(ov));
-        if (srow) srow[idx] = pack8(v[i]);
+        if (kMode != kModeQuant && out_amax) amax = max(amax, amax8(ov));
+        if (kMode == kModeQuant) {
+          const uint32_t w[4] = {ov.x, ov.y, ov.z, ov.w};
+          uint32_t q[2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * t]));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * t + 1]));
+            float2 c0, c1;
+            c0.x = fminf(fmaxf(f0.x * qinv, -kMx), kMx);
+            c0.y = fminf(fmaxf(f0.y * qinv, -kMx), kMx);
+            c1.x = fminf(fmaxf(f1.x * qinv, -kMx), kMx);
+            c1.y = fminf(fmaxf(f1.y * qinv, -kMx), kMx);
+            const __nv_fp8_interpretation_t it = kFmt == WBK_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2;
+            q[t] = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(c0, __NV_SATFINITE, it)) |
+                   (static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(c1, __NV_SATFINITE, it)) << 16);
+          }
+          reinterpret_cast<uint2*>(q_out + row * D)[idx] = make_uint2(q[0], q[1]);
+        }
       }
     }
   }
-  if (out_amax) block_amax_commit(amax, out_amax);
+  if (kMode != kModeQuant && out_amax) block_amax_commit(amax, out_amax);
 }
 
 // CTA per row, for D > 32*8*16. Three reads of the row (L2-resident).
@@ -242,7 +302,8 @@ int launch_norm(const void* x, const void* res, const void* gamma, const void* b
   const int grid = static_cast<int>(want < sms * 4 ? want : sms * 4);
 #define WBK_NORM_CASE(V)                                                                       \
   if (nvec <= 32 * (V)) {                                                                      \
-    norm_warp_kernel<V, kRms><<<grid, kThreads, 0, s>>>(xh, rh, gh, bh, oh, sh, rows, d, eps, out_amax); \
+    norm_warp_kernel<V, kRms, kModeNormal, 0><<<grid, kThreads, 0, s>>>(xh, rh, gh, bh, oh, sh, rows, d, eps,  \
+                                                                      out_amax, nullptr, nullptr, nullptr, nullptr); \
     return cuda_check(cudaGetLastError(), "norm kernel launch");                               \
   }
   WBK_NORM_CASE(1)
@@ -258,6 +319,35 @@ int launch_norm(const void* x, const void* res, const void* gamma, const void* b
   const int bgrid = static_cast<int>(rows < sms * 8 ? rows : sms * 8);
   norm_block_kernel<kRms><<<bgrid, kThreads, 0, s>>>(xh, rh, gh, bh, oh, sh, rows, d, eps, out_amax);
   return cuda_check(cudaGetLastError(), "norm kernel launch");
+}
+
+// Fused LayerNorm -> FP8 quantise, D <= 32*8*16 (warp-per-row kernel only, so
+// the stats pass and the quantise pass run the same per-row arithmetic).
+template <int kMode, int kFmt>
+int launch_ln_mode(const __half* x, const __half* gamma, const __half* beta, int64_t rows, int D, float eps,
+                   uint32_t* amax, float2* stats, const float* scale_inv, uint8_t* q, float* scale_out, cudaStream_t s) {
+  const int nvec = D / 8;
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t want = (rows + kWarps - 1) / kWarps;
+  const int grid = static_cast<int>(want < sms * 4 ? want : sms * 4);
+#define WBK_LNQ_CASE(V)                                                                                  \
+  if (nvec <= 32 * (V)) {                                                                                \
+    norm_warp_kernel<V, false, kMode, kFmt><<<grid, kThreads, 0, s>>>(x, nullptr, gamma, beta, nullptr, \
+                                                                      nullptr, rows, D, eps, amax,       \
+                                                                      stats, scale_inv, q, scale_out);   \
+    return cuda_check(cudaGetLastError(), "layernorm-quantise launch");                                 \
+  }
+  WBK_LNQ_CASE(1)
+  WBK_LNQ_CASE(2)
+  WBK_LNQ_CASE(3)
+  WBK_LNQ_CASE(4)
+  WBK_LNQ_CASE(5)
+  WBK_LNQ_CASE(6)
+  WBK_LNQ_CASE(8)
+  WBK_LNQ_CASE(12)
+  WBK_LNQ_CASE(16)
+#undef WBK_LNQ_CASE
+  return fail(WBK_ERR_UNSUPPORTED, "wbk_layernorm_quantise_f16: D=%d exceeds 4096", D);
 }
 
 int check_norm_args(const char* who, const void* x, const void* res, const void* gamma, const void* beta, const void* out,
@@ -296,6 +386,44 @@ int wbk_rmsnorm_f16(const void* x, const void* residual, const void* gamma, void
   if (rows == 0) return WBK_OK;
   return launch_norm<true>(x, residual, gamma, nullptr, out, nullptr, rows, D, eps, nullptr,
                            reinterpret_cast<cudaStream_t>(stream));
+}
+
+int64_t wbk_layernorm_quantise_ws_bytes(int64_t rows) {
+  return (rows > 0 ? rows : 0) * static_cast<int64_t>(sizeof(float2)) + 16;
+}
+
+int wbk_layernorm_quantise_f16(const void* x, const void* gamma, const void* beta, int64_t rows, int64_t D, float eps,
+                               int fmt, void* q_out, float* scale_out, void* ws, uint32_t* amax_ws,
+                               wbk_stream_t stream) {
+  if (fmt != WBK_FMT_E4M3 && fmt != WBK_FMT_E5M2)
+    return fail(WBK_ERR_INVALID_ARG, "wbk_layernorm_quantise_f16: unknown fp8 format %d", fmt);
+  if (int e = check_norm_args("wbk_layernorm_quantise_f16", x, nullptr, gamma, beta, q_out, nullptr, rows, D, true))
+    return e;
+  if (D > 4096) return fail(WBK_ERR_UNSUPPORTED, "wbk_layernorm_quantise_f16: D=%lld exceeds 4096", (long long)D);
+  if (ws == nullptr || amax_ws == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_layernorm_quantise_f16: null workspace");
+  if (!aligned(ws, 16)) return fail(WBK_ERR_INVALID_ARG, "wbk_layernorm_quantise_f16: ws must be 16-byte aligned");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  float2* stats = static_cast<float2*>(ws);
+  float* scale_inv = reinterpret_cast<float*>(static_cast<char*>(ws) + rows * sizeof(float2));
+  if (int e = cuda_check(cudaMemsetAsync(amax_ws, 0, sizeof(uint32_t), s), "wbk_layernorm_quantise_f16 memset"))
+    return e;
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* gh = static_cast<const __half*>(gamma);
+  const __half* bh = static_cast<const __half*>(beta);
+  uint8_t* q = static_cast<uint8_t*>(q_out);
+  const int d = static_cast<int>(D);
+  if (rows > 0) {
+    if (int e = launch_ln_mode<kModeStats, WBK_FMT_E4M3>(xh, gh, bh, rows, d, eps, amax_ws, stats, nullptr, nullptr,
+                                                          nullptr, s))
+      return e;
+  }
+  if (int e = wbk_scale_from_amax(amax_ws, fmt, scale_inv, stream)) return e;
+  if (rows == 0) return WBK_OK;  // scale only (1.0); scale_out is left unwritten like an empty quantise
+  return fmt == WBK_FMT_E4M3
+             ? launch_ln_mode<kModeQuant, WBK_FMT_E4M3>(xh, gh, bh, rows, d, eps, nullptr, stats, scale_inv, q,
+                                                         scale_out, s)
+             : launch_ln_mode<kModeQuant, WBK_FMT_E5M2>(xh, gh, bh, rows, d, eps, nullptr, stats, scale_inv, q,
+                                                         scale_out, s);
 }
 
 }  // extern "C"

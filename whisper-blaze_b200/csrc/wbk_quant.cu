@@ -139,6 +139,16 @@ quantise_f16_kernel(const __half* __restrict__ x, int64_t n, const uint32_t* __r
   }
 }
 
+// One thread: scale_inv[0] = scale, scale_inv[1] = 1/scale, from an amax (the
+// same rule and the same compiled division as the quantise kernels above).
+__global__ void scale_from_amax_kernel(const uint32_t* __restrict__ amax_bits, float max_fp8,
+                                       float* __restrict__ scale_inv) {
+  float scale, inv;
+  scale_from_amax(*amax_bits, max_fp8, scale, inv);
+  scale_inv[0] = scale;
+  scale_inv[1] = inv;
+}
+
 // ------------------------------------------------------- GELU + quantise
 //
 // The FFN activation of the encoder is quantised right after the GELU. Here
@@ -480,6 +490,13 @@ int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out, float* scal
   if (int e = cuda_check(cudaMemsetAsync(amax_ws, 0, sizeof(uint32_t), s), "wbk_quantise_f16 memset")) return e;
   if (int e = wbk_amax_f16(x, n, amax_ws, stream)) return e;
   return wbk_quantise_from_amax_f16(x, n, fmt, amax_ws, q_out, scale_out, stream);
+}
+
+int wbk_scale_from_amax(const uint32_t* amax_bits, int fmt, float* scale_inv, wbk_stream_t stream) {
+  if (int e = check_fmt(fmt)) return e;
+  if (amax_bits == nullptr || scale_inv == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_scale_from_amax: null pointer");
+  scale_from_amax_kernel<<<1, 1, 0, reinterpret_cast<cudaStream_t>(stream)>>>(amax_bits, fmt_max(fmt), scale_inv);
+  return cuda_check(cudaGetLastError(), "wbk_scale_from_amax launch");
 }
 
 int wbk_quantise_gelu_f16(const void* y, int64_t n, int fmt, const uint32_t* ymax_key, void* q_out,

@@ -44,6 +44,9 @@ _PROTOTYPES = {
     "wbk_quantise_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "wbk_quantise_f16_noalloc": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp]),
     "wbk_quantise_gelu_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "wbk_scale_from_amax": (_i32, [_vp, _i32, _vp, _vp]),
+    "wbk_layernorm_quantise_f16": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _i32, _vp, _vp, _vp, _vp, _vp]),
+    "wbk_layernorm_quantise_ws_bytes": (_i64, [_i64]),
     "wbk_dequantise_f16": (_i32, [_vp, _i64, _i32, _f32, _vp, _vp]),
     "wbk_layernorm_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp, _vp]),
     "wbk_rmsnorm_f16": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
@@ -84,7 +87,7 @@ def header_symbols() -> list[str]:
     """Names of every entry point declared in include/wbk.h."""
     with open(HEADER_PATH) as f:
         text = f.read()
-    return sorted(set(re.findall(r"^\s*(?:const\s+char\*|int)\s+(wbk_\w+)\s*\(", text, flags=re.M)))
+    return sorted(set(re.findall(r"^\s*(?:const\s+char\s*\*|int64_t|int)\s+(wbk_\w+)\s*\(", text, flags=re.M)))
 
 
 def check(status: int, what: str) -> None:

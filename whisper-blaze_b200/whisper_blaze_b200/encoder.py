@@ -8,14 +8,13 @@ fp16 (the reference's own attention: HF runs it through torch SDPA).
 
 Per layer, on one stream and without any host synchronisation:
 
-  LN1(h)            -> x   (fp16) + amax(x)            norm kernel
-  quantise(x)       -> xq  (fp8)  + scale              quantise kernel
+  LN1(h) -> fp8     -> xq  (fp8)  + scale              norm stats pass + norm quantise pass
+                                                       (the fp16 LN output is never stored)
   QKV GEMM          -> qkv (fp16), bias epilogue       tcgen05 GEMM
   SDPA(q, k, v)     -> a   (fp16)                      torch
   amax+quantise(a)  -> aq  (fp8)                       2 kernels
   out-proj GEMM     -> h2 = fp16(acc*s + b + h)        residual epilogue
-  LN2(h2)           -> x2  + amax(x2)                  norm kernel
-  quantise(x2)      -> x2q                             quantise kernel
+  LN2(h2) -> fp8    -> x2q                             norm stats pass + norm quantise pass
   fc1 GEMM          -> y = fp16(acc*s + b) + max(y)          bias + max-key epilogue
   gelu+quantise(y)  -> fq = q8(fp16(gelu(y)))              (amax of the GELU output from max(y))
   fc2 GEMM          -> h' = fp16(clamp(acc*s + b + h2))      residual+clamp epilogue
@@ -163,6 +162,7 @@ class FP8EncoderStack:
         self.fq = e(T, Fd, dt=torch.uint8)
         self.out = e(T, D)
         self.amax = torch.zeros(8, dtype=torch.int32, device=dev)
+        self.ln_ws = ops.layernorm_quantise_ws(T, dev)
         self.scales = torch.ones(4, dtype=torch.float32, device=dev)
         self._ws_tokens = T
 
@@ -196,9 +196,11 @@ class FP8EncoderStack:
         amax, sc = self.amax, self.scales
         keep = (lambda k, t: capture.__setitem__(k, t.clone())) if capture is not None else (lambda k, t: None)
         amax.zero_()
-        ops.layernorm(h, None, L.ln1_g, L.ln1_b, cfg.eps, out=self.x, out_amax=amax[0:1])
-        ops.quantise_from_amax(self.x, amax[0:1], q_out=self.xq, scale_out=sc[0:1])
-        keep("ln1", self.x), keep("ln1_q", self.xq), keep("ln1_s", sc[0:1])
+        ops.layernorm_quantise(h, L.ln1_g, L.ln1_b, cfg.eps, q_out=self.xq, scale_out=sc[0:1], ws=self.ln_ws,
+                               amax_ws=amax[0:1])
+        if capture is not None:
+            keep("ln1", ops.layernorm(h, None, L.ln1_g, L.ln1_b, cfg.eps)[0])
+        keep("ln1_q", self.xq), keep("ln1_s", sc[0:1])
         self._gemm("qkv", 2 * T * D * 3 * D, self.xq, sc[0:1], L.w_qkv, L.s_qkv, L.b_qkv, out=self.qkv)
         keep("qkv", self.qkv)
         attn = self._attention(B, S)
@@ -208,9 +210,11 @@ class FP8EncoderStack:
         self._gemm("out_proj", 2 * T * D * D, self.aq, sc[1:2], L.w_o, L.s_o, L.b_o, residual=h,
                    epilogue="residual", out=self.h2)
         keep("h2", self.h2)
-        ops.layernorm(self.h2, None, L.ln2_g, L.ln2_b, cfg.eps, out=self.x, out_amax=amax[2:3])
-        ops.quantise_from_amax(self.x, amax[2:3], q_out=self.xq, scale_out=sc[2:3])
-        keep("ln2", self.x), keep("ln2_q", self.xq), keep("ln2_s", sc[2:3])
+        ops.layernorm_quantise(self.h2, L.ln2_g, L.ln2_b, cfg.eps, q_out=self.xq, scale_out=sc[2:3],
+                               ws=self.ln_ws, amax_ws=amax[2:3])
+        if capture is not None:
+            keep("ln2", ops.layernorm(self.h2, None, L.ln2_g, L.ln2_b, cfg.eps)[0])
+        keep("ln2_q", self.xq), keep("ln2_s", sc[2:3])
         self._gemm("fc1", 2 * T * D * Fd, self.xq, sc[2:3], L.w_fc1, L.s_fc1, L.b_fc1, epilogue="bias_maxkey",
                    out=self.f, out_amax=amax[3:4])
         ops.quantise_gelu(self.f, amax[3:4], q_out=self.fq, scale_out=sc[3:4], amax_ws=amax[4:5])

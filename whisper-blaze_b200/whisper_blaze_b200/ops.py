@@ -192,6 +192,43 @@ def layernorm(x: torch.Tensor, residual: Optional[torch.Tensor], gamma: torch.Te
     return o, s
 
 
+def layernorm_quantise_ws(rows: int, device) -> torch.Tensor:
+    """Workspace for layernorm_quantise: per-row statistics + the (scale, 1/scale) pair."""
+    return torch.empty(int(lib().wbk_layernorm_quantise_ws_bytes(int(rows))), dtype=torch.uint8, device=device)
+
+
+def layernorm_quantise(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float = 1e-5, fmt="e4m3",
+                       q_out: Optional[torch.Tensor] = None, scale_out: Optional[torch.Tensor] = None,
+                       ws: Optional[torch.Tensor] = None,
+                       amax_ws: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp8 codes of LayerNorm(x) (no residual), bit-identical to layernorm() then quantise(),
+    without writing the fp16 LayerNorm output."""
+    require_input(x, "x")
+    require_input(gamma, "gamma")
+    require_input(beta, "beta")
+    require_fp16(x, "x")
+    require_fp16(gamma, "gamma")
+    require_fp16(beta, "beta")
+    D = x.shape[-1]
+    if gamma.numel() != D or beta.numel() != D:
+        raise RuntimeError(f"gamma and beta must have {D} elements")
+    rows = x.numel() // D if D else 0
+    f = fmt_code(fmt)
+    q = torch.empty(x.shape, dtype=torch.uint8, device=x.device) if q_out is None else q_out
+    s = torch.empty(1, dtype=torch.float32, device=x.device) if scale_out is None else scale_out
+    w = layernorm_quantise_ws(rows, x.device) if ws is None else ws
+    a = torch.empty(1, dtype=torch.int32, device=x.device) if amax_ws is None else amax_ws
+    if w.numel() < lib().wbk_layernorm_quantise_ws_bytes(rows):
+        raise RuntimeError("layernorm_quantise workspace too small")
+    require_same_device(x, gamma, beta, q, s, w, a)
+    with torch.cuda.device(x.device):
+        check(lib().wbk_layernorm_quantise_f16(x.data_ptr(), gamma.data_ptr(), beta.data_ptr(), rows, D, float(eps), f,
+                                               q.data_ptr(), s.data_ptr(), w.data_ptr(), a.data_ptr(), stream_of(x)),
+              "layernorm_quantise")
+    _count(2)
+    return q, s
+
+
 def rmsnorm(x: torch.Tensor, residual: torch.Tensor, gamma: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
     require_input(x, "x")
     require_input(residual, "residual")
