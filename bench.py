@@ -230,7 +230,7 @@ def run_stack(args, world, rank, local):
             w_qkv=n(3 * D, D), b_qkv=b_qkv, w_o=n(D, D), b_o=n(D),
             ln2_g=torch.ones(D, dtype=torch.float16, device=dev), ln2_b=torch.zeros(D, dtype=torch.float16, device=dev),
             w_fc1=n(Fd, D), b_fc1=n(Fd), w_fc2=n(D, Fd), b_fc2=n(D)))
-    stack = FP8EncoderStack(cfg, layers, dev)
+    stack = FP8EncoderStack(cfg, layers, dev, slice_chunks=args.slice_chunks or None)
     del layers
 
     start, stop = shard_bounds(TOTAL_CHUNKS, world, rank)
@@ -240,7 +240,7 @@ def run_stack(args, world, rank, local):
     x = torch.randn(local_b, cfg.seq_len, D, generator=gx, device=dev, dtype=torch.float32).half()
 
     def step():
-        y = stack.forward(x)
+        y = stack.forward_graphed(x) if args.graph else stack.forward(x)
         if world > 1:
             return gather_batch(y, TOTAL_CHUNKS)
         return y
@@ -252,7 +252,8 @@ def run_stack(args, world, rank, local):
 
     stream = torch.cuda.current_stream(dev)
     launches0 = ops.LAUNCHES[0]
-    stack.gemm_timings = []
+    if not args.graph:
+        stack.gemm_timings = []
     with ClockSampler(local) as clocks:
         barrier(world)
         torch.cuda.synchronize()
@@ -266,8 +267,20 @@ def run_stack(args, world, rank, local):
         torch.cuda.cudart().cudaProfilerStop()
         barrier(world)
     launches = ops.LAUNCHES[0] - launches0
+    if args.graph:
+        # a replay issues the captured launches without passing through Python: count one eager step's
+        launches = (stack.launches_per_forward or 0) * args.steps
     ms_local = t0.elapsed_time(t1) / args.steps
     ms = max_over_ranks(ms_local, world, dev)
+    roofline_steps = args.steps
+    if args.graph:
+        # Kernel-level timing for the roofline: CUDA events bracket every GEMM launch of
+        # eager steps run right after the timed graph replays (same kernels, same shapes).
+        roofline_steps = max(1, min(args.steps, 3))
+        stack.gemm_timings = []
+        for _ in range(roofline_steps):
+            stack.forward(x)
+        torch.cuda.synchronize()
     gemm_ms = sum(t.ms() for t in stack.gemm_timings)
     gemm_flops = sum(t.flops for t in stack.gemm_timings)
     n_gemm = len(stack.gemm_timings)
@@ -276,7 +289,7 @@ def run_stack(args, world, rank, local):
         b = breakdown.setdefault(t.name, {"ms": 0.0, "flops": 0.0})
         b["ms"] += t.ms()
         b["flops"] += t.flops
-    breakdown = {k: {"ms_per_step": v["ms"] / args.steps, "tflops": v["flops"] / (v["ms"] * 1e-3) / 1e12}
+    breakdown = {k: {"ms_per_step": v["ms"] / roofline_steps, "tflops": v["flops"] / (v["ms"] * 1e-3) / 1e12}
                  for k, v in breakdown.items()}
     stack.gemm_timings = None
     clock_info = clocks.summary()
@@ -287,8 +300,8 @@ def run_stack(args, world, rank, local):
     e2e_steps = max(1, min(args.steps, 5))
 
     def e2e_step():
-        dev_in = x_host.to(dev, non_blocking=True)
-        y = stack.forward(dev_in)
+        dev_in = stack.device_input(x_host)
+        y = stack.forward_graphed(dev_in) if args.graph else stack.forward(dev_in)
         full = gather_batch(y, TOTAL_CHUNKS) if world > 1 else y
         if rank == 0:
             out_host.copy_(full, non_blocking=True)
@@ -330,6 +343,7 @@ def run_stack(args, world, rank, local):
             "config": {"workload": "encoder_stack (config 5)", "global_batch": TOTAL_CHUNKS,
                        "seq_len": cfg.seq_len, "d_model": D, "heads": cfg.heads, "ffn": Fd, "layers": cfg.layers,
                        "parallelism": f"batch-sharded dp{world}, NCCL all_gather of outputs",
+                       "slice_chunks": args.slice_chunks, "cuda_graph": bool(args.graph),
                        "l2": "inputs and every activation > 126 MB L2 (no flush needed)"},
             "e2e": {"value": TOTAL_CHUNKS / (e2e_ms * 1e-3), "unit": "chunks/s",
                     "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h)},
@@ -337,8 +351,11 @@ def run_stack(args, world, rank, local):
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved else None, "peak_source": peak_src,
                          "frac_of_nominal_fp8_4500": (achieved / NOMINAL_FP8_TFLOPS) if achieved else None,
-                         "gemm_launches_timed": n_gemm, "gemm_ms_per_step": gemm_ms / args.steps,
-                         "gemm_share_of_step": (gemm_ms / args.steps) / ms_local,
+                         "gemm_launches_timed": n_gemm, "gemm_ms_per_step": gemm_ms / roofline_steps,
+                         "gemm_share_of_step": (gemm_ms / roofline_steps) / ms_local,
+                         "gemm_timing": ("CUDA events around each GEMM launch of " +
+                                         (f"{roofline_steps} eager steps right after the timed graph replays"
+                                          if args.graph else "the timed steps")),
                          "gemm_breakdown": breakdown,
                          "traffic": roofline_traffic("fp8_gemm_stack")},
             "gpu_launches": launches,
@@ -431,6 +448,9 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--ref-step-budget", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", type=int, default=1, help="replay the stack from a CUDA graph (1) or launch eagerly (0)")
+    ap.add_argument("--slice-chunks", type=int, default=int(os.environ.get("WBK_SLICE_CHUNKS", "0")),
+                    help="chunks per pass through the stack (0 = the whole per-GPU batch at once)")
     args = ap.parse_args()
     world, rank, local = setup_dist()
     try:

@@ -127,8 +127,14 @@ class FP8EncoderStack:
     """Encoder stack on one GPU. forward() takes [B, S, D] fp16 on the device."""
 
     def __init__(self, cfg: EncoderConfig, layers: List[LayerWeights], device,
-                 final_ln: Optional[tuple] = None) -> None:
+                 final_ln: Optional[tuple] = None, slice_chunks: Optional[int] = None) -> None:
+        """slice_chunks: run the batch through the whole stack this many chunks at a
+        time (None = all at once). Smaller slices keep each slice's [tokens, d_model]
+        tensors (1500 x 1280 x 2 B = 3.84 MB per chunk) inside the 126 MB L2, so the
+        passes that read a tensor twice (LayerNorm statistics then quantise,
+        amax then quantise) hit L2 on the second read."""
         self.cfg = cfg
+        self.slice_chunks = slice_chunks
         self.device = torch.device(device)
         self.layers: List[_QuantLayer] = []
         with torch.cuda.device(self.device):
@@ -147,6 +153,11 @@ class FP8EncoderStack:
             self.final_b = final_ln[1].to(self.device)
         self._ws_tokens = -1
         self.gemm_timings: Optional[List[GemmTiming]] = None  # set to [] to record
+        self._graph = None
+        self._graph_key = None
+        self.launches_per_forward: Optional[int] = None  # libwbk launches of the last eager forward
+        self._graph_out = None
+        self._host_in = None
 
     # -------------------------------------------------------------- buffers
     def _workspace(self, T: int) -> None:
@@ -177,17 +188,17 @@ class FP8EncoderStack:
         return out
 
     # -------------------------------------------------------------- compute
-    def _attention(self, B: int, S: int) -> torch.Tensor:
+    def _attention(self, qkv_buf: torch.Tensor, attn_buf: torch.Tensor, B: int, S: int) -> torch.Tensor:
         cfg = self.cfg
         H, Dh = cfg.heads, cfg.head_dim
-        qkv = self.qkv.view(B, S, 3, H, Dh)
+        qkv = qkv_buf.view(B, S, 3, H, Dh)
         q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
         o = F.scaled_dot_product_attention(q, k, v)  # [B, H, S, Dh]
         o = o.transpose(1, 2)
         if o.is_contiguous():
             return o.reshape(B * S, cfg.d_model)
-        self.attn.view(B, S, H, Dh).copy_(o)
-        return self.attn
+        attn_buf.view(B, S, H, Dh).copy_(o)
+        return attn_buf
 
     def _layer(self, L: _QuantLayer, h: torch.Tensor, h_next: torch.Tensor, B: int, S: int,
                capture: Optional[dict] = None) -> None:
@@ -195,31 +206,34 @@ class FP8EncoderStack:
         T, D, Fd = B * S, cfg.d_model, cfg.ffn
         amax, sc = self.amax, self.scales
         keep = (lambda k, t: capture.__setitem__(k, t.clone())) if capture is not None else (lambda k, t: None)
+        # row views of the workspace for this slice (T <= the rows the workspace was sized for)
+        xq, aq, qkv, h2, f, fq, attn_buf = (b[:T] for b in (self.xq, self.aq, self.qkv, self.h2, self.f, self.fq,
+                                                             self.attn))
         amax.zero_()
-        ops.layernorm_quantise(h, L.ln1_g, L.ln1_b, cfg.eps, q_out=self.xq, scale_out=sc[0:1], ws=self.ln_ws,
+        ops.layernorm_quantise(h, L.ln1_g, L.ln1_b, cfg.eps, q_out=xq, scale_out=sc[0:1], ws=self.ln_ws,
                                amax_ws=amax[0:1])
         if capture is not None:
             keep("ln1", ops.layernorm(h, None, L.ln1_g, L.ln1_b, cfg.eps)[0])
-        keep("ln1_q", self.xq), keep("ln1_s", sc[0:1])
-        self._gemm("qkv", 2 * T * D * 3 * D, self.xq, sc[0:1], L.w_qkv, L.s_qkv, L.b_qkv, out=self.qkv)
-        keep("qkv", self.qkv)
-        attn = self._attention(B, S)
+        keep("ln1_q", xq), keep("ln1_s", sc[0:1])
+        self._gemm("qkv", 2 * T * D * 3 * D, xq, sc[0:1], L.w_qkv, L.s_qkv, L.b_qkv, out=qkv)
+        keep("qkv", qkv)
+        attn = self._attention(qkv, attn_buf, B, S)
         ops.amax_accumulate(attn, amax[1:2])
-        ops.quantise_from_amax(attn, amax[1:2], q_out=self.aq, scale_out=sc[1:2])
-        keep("attn", attn), keep("attn_q", self.aq), keep("attn_s", sc[1:2])
-        self._gemm("out_proj", 2 * T * D * D, self.aq, sc[1:2], L.w_o, L.s_o, L.b_o, residual=h,
-                   epilogue="residual", out=self.h2)
-        keep("h2", self.h2)
-        ops.layernorm_quantise(self.h2, L.ln2_g, L.ln2_b, cfg.eps, q_out=self.xq, scale_out=sc[2:3],
+        ops.quantise_from_amax(attn, amax[1:2], q_out=aq, scale_out=sc[1:2])
+        keep("attn", attn), keep("attn_q", aq), keep("attn_s", sc[1:2])
+        self._gemm("out_proj", 2 * T * D * D, aq, sc[1:2], L.w_o, L.s_o, L.b_o, residual=h,
+                   epilogue="residual", out=h2)
+        keep("h2", h2)
+        ops.layernorm_quantise(h2, L.ln2_g, L.ln2_b, cfg.eps, q_out=xq, scale_out=sc[2:3],
                                ws=self.ln_ws, amax_ws=amax[2:3])
         if capture is not None:
-            keep("ln2", ops.layernorm(self.h2, None, L.ln2_g, L.ln2_b, cfg.eps)[0])
-        keep("ln2_q", self.xq), keep("ln2_s", sc[2:3])
-        self._gemm("fc1", 2 * T * D * Fd, self.xq, sc[2:3], L.w_fc1, L.s_fc1, L.b_fc1, epilogue="bias_maxkey",
-                   out=self.f, out_amax=amax[3:4])
-        ops.quantise_gelu(self.f, amax[3:4], q_out=self.fq, scale_out=sc[3:4], amax_ws=amax[4:5])
-        keep("fc1", self.f), keep("fc1_q", self.fq), keep("fc1_s", sc[3:4])
-        self._gemm("fc2", 2 * T * Fd * D, self.fq, sc[3:4], L.w_fc2, L.s_fc2, L.b_fc2, residual=self.h2,
+            keep("ln2", ops.layernorm(h2, None, L.ln2_g, L.ln2_b, cfg.eps)[0])
+        keep("ln2_q", xq), keep("ln2_s", sc[2:3])
+        self._gemm("fc1", 2 * T * D * Fd, xq, sc[2:3], L.w_fc1, L.s_fc1, L.b_fc1, epilogue="bias_maxkey",
+                   out=f, out_amax=amax[3:4])
+        ops.quantise_gelu(f, amax[3:4], q_out=fq, scale_out=sc[3:4], amax_ws=amax[4:5])
+        keep("fc1", f), keep("fc1_q", fq), keep("fc1_s", sc[3:4])
+        self._gemm("fc2", 2 * T * Fd * D, fq, sc[3:4], L.w_fc2, L.s_fc2, L.b_fc2, residual=h2,
                    epilogue="residual_clamp", out=h_next)
         keep("out", h_next)
 
@@ -237,28 +251,71 @@ class FP8EncoderStack:
         B, S, D = hidden.shape
         if D != self.cfg.d_model:
             raise RuntimeError(f"hidden size {D} != d_model {self.cfg.d_model}")
-        T = B * S
+        step = B if not self.slice_chunks else min(B, self.slice_chunks)
+        launches0 = ops.LAUNCHES[0]
         with torch.cuda.device(self.device):
-            self._workspace(T)
-            h = hidden.reshape(T, D)
-            bufs = (self.h_a, self.h_b)
-            for i, L in enumerate(self.layers):
-                nxt = bufs[i % 2]
-                cap = None
-                if capture is not None:
-                    cap = {"in": h.clone()}
-                    capture.append(cap)
-                self._layer(L, h, nxt, B, S, cap)
-                h = nxt
-            o = self.out if out is None else out.view(T, D)
-            ops.layernorm(h, None, self.final_g, self.final_b, self.cfg.eps, out=o)
-        return o.view(B, S, D)
+            self._workspace(step * S)
+            if out is None:
+                if step == B:
+                    o_full = self.out
+                else:
+                    o_full = torch.empty(B * S, D, dtype=torch.float16, device=self.device)
+            else:
+                o_full = out.view(B * S, D)
+            for b0 in range(0, B, step):
+                nb = min(step, B - b0)
+                T = nb * S
+                h = hidden[b0:b0 + nb].reshape(T, D)
+                bufs = (self.h_a[:T], self.h_b[:T])
+                for i, L in enumerate(self.layers):
+                    nxt = bufs[i % 2]
+                    cap = None
+                    if capture is not None:
+                        cap = {"in": h.clone()}
+                        capture.append(cap)
+                    self._layer(L, h, nxt, nb, S, cap)
+                    h = nxt
+                ops.layernorm(h, None, self.final_g, self.final_b, self.cfg.eps, out=o_full[b0 * S:b0 * S + T])
+        self.launches_per_forward = ops.LAUNCHES[0] - launches0
+        return o_full.view(B, S, D)
 
     @torch.inference_mode()
-    def forward_host(self, hidden_host: torch.Tensor, out_host: Optional[torch.Tensor] = None) -> torch.Tensor:
+    def forward_graphed(self, hidden: torch.Tensor) -> torch.Tensor:
+        """forward() replayed from a CUDA graph: the ~36 launches per layer cost one
+        graph launch. The graph is captured on the first call for a given input
+        tensor (address and shape) and replayed on later calls with the same
+        tensor; the returned output lives in the graph's memory and is
+        overwritten by the next replay."""
+        ops.require_input(hidden, "hidden")
+        key = (hidden.data_ptr(), tuple(hidden.shape), hidden.device)
+        if self._graph is None or self._graph_key != key:
+            self._graph = None
+            with torch.cuda.device(self.device):
+                self.forward(hidden)  # sizes the workspace and runs every lazy initialisation
+                torch.cuda.synchronize(self.device)
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    y = self.forward(hidden)
+                torch.cuda.synchronize(self.device)
+            self._graph, self._graph_key, self._graph_out = g, key, y
+        self._graph.replay()
+        return self._graph_out
+
+    def device_input(self, hidden_host: torch.Tensor) -> torch.Tensor:
+        """Copy a (pinned) host batch into this stack's persistent device input buffer
+        (asynchronously, on the current stream) and return that buffer — the same
+        tensor every call, so a graphed forward on it is captured once."""
+        if self._host_in is None or self._host_in.shape != hidden_host.shape:
+            self._host_in = torch.empty(hidden_host.shape, dtype=torch.float16, device=self.device)
+        self._host_in.copy_(hidden_host, non_blocking=True)
+        return self._host_in
+
+    @torch.inference_mode()
+    def forward_host(self, hidden_host: torch.Tensor, out_host: Optional[torch.Tensor] = None,
+                     graphed: bool = False) -> torch.Tensor:
         """Host-to-host call: copy in (from pinned memory), run, copy out."""
-        dev_in = hidden_host.to(self.device, non_blocking=True)
-        y = self.forward(dev_in)
+        dev_in = self.device_input(hidden_host)
+        y = self.forward_graphed(dev_in) if graphed else self.forward(dev_in)
         if out_host is None:
             out_host = torch.empty(y.shape, dtype=y.dtype, pin_memory=True)
         out_host.copy_(y, non_blocking=True)
