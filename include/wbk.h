@@ -90,7 +90,8 @@ int wbk_quantise_from_amax_f16(const void* x, int64_t n, int fmt,
 
 /* Convenience: zero *amax_ws, accumulate amax, then quantise (three stream
  * operations, no host synchronisation). amax_ws is a caller-owned device
- * uint32 used as the accumulator.
+ * uint32 used as the accumulator; it ends holding the amax bits. Tensors of
+ * up to 262144 elements take one single-CTA launch instead (same results).
  * Replaces: quantise_to_e4m3 / quantise_to_e5m2, fp8_quantize.cu:222-257
  * (without its device->host copy of per-block partials, fp8_quantize.cu:212). */
 int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out,

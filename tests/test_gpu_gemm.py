@@ -1,5 +1,8 @@
 """GPU parity of the tcgen05 FP8 GEMM (calls go through the C ABI).
 
+Shapes cover the three tile widths the host picks (64 for M <= 128, 128 when
+256-wide tiles would leave SMs idle, 256 otherwise).
+
 Gate (north star): max relative error <= 1e-2, defined as
 max|y - ref| / max|ref| over the output, against the fp32 matmul of the same
 dequantised operands (oracle/gemm.py); elementwise also
@@ -54,6 +57,8 @@ SHAPES = [
     (1, 256, 128), (63, 8, 16), (65, 24, 48), (129, 264, 272), (300, 1000, 1280),
     (256, 1280, 5120),    # fc2 K
     (130, 136, 4096 + 16),  # K not a multiple of the 128-byte stage
+    (4096, 2560, 1280),   # enough tiles for the 256-wide tile path
+    (4224 + 7, 2568, 384),  # 256-wide tiles with ragged M and N edges
 ]
 
 
@@ -75,7 +80,7 @@ def test_gemm_vocab_projection(cuda_device):
 
 @pytest.mark.parametrize("epi,name", [(gemm.EPI_GELU, "gelu"), (gemm.EPI_RESIDUAL, "residual"),
                                       (gemm.EPI_RESIDUAL_CLAMP, "residual_clamp")])
-@pytest.mark.parametrize("M,N,K", [(384, 5120, 1280), (200, 1280, 1280), (77, 40, 64)])
+@pytest.mark.parametrize("M,N,K", [(384, 5120, 1280), (200, 1280, 1280), (77, 40, 64), (4096, 2560, 640)])
 def test_gemm_epilogues(cuda_device, epi, name, M, N, K):
     aq, sa, wq, sw, b = _operands(M, N, K, 31 + M, cuda_device)
     res = randn_f16((M, N), 33).to(cuda_device) if epi != gemm.EPI_GELU else None

@@ -219,3 +219,15 @@ def test_quantise_gelu_negative_side_amax(cuda_device):
     _check_gelu_quant(y, q, s)
     g = ogemm.gelu_f16(y).float()
     assert abs(s.item() * 448.0 - g.abs().max().item()) <= 2e-3 * g.abs().max().item()
+
+
+@pytest.mark.parametrize("n", [1, 4099, 81920, 262144, 262145])
+def test_small_tensor_path_matches_two_kernel_path(cuda_device, n):
+    """wbk_quantise_f16 takes a single-CTA path up to 262144 elements; it must give the bytes and scale
+    of the amax kernel + quantise kernel pair."""
+    x = randn_f16((n,), 400 + n % 97, std=3.0).to(cuda_device)
+    q, s = ops.quantise(x)
+    ws = ops.new_amax_ws(cuda_device)
+    ops.amax_accumulate(x, ws)
+    q2, s2 = ops.quantise_from_amax(x, ws)
+    assert torch.equal(q, q2) and s.view(torch.int32).item() == s2.view(torch.int32).item()

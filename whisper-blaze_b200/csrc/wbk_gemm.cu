@@ -47,19 +47,33 @@ __device__ uint32_t g_device_error;  // first device-side error: code | site << 
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 128;  // bytes of K per stage = fp8 elements = one 128-byte swizzle row
 constexpr int UMMA_K = 32;
-constexpr int STAGES = 4;
 constexpr int A_STAGE_BYTES = BM * BK;  // 16 KB
-constexpr int B_STAGE_BYTES = BN * BK;  // 32 KB
 constexpr int NUM_ACC = 2;
-constexpr int TMEM_COLS = NUM_ACC * BN;  // 512
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + EPI_WARPS * 32;  // 320
-constexpr int EPI_COLS = BN / 2;              // columns per epilogue warp
 constexpr int CHUNK = 32;                     // columns per tcgen05.ld / per TMA store box
 constexpr int STAGE_OUT_BYTES = 32 * CHUNK * 2;  // 32 rows x 32 fp16 = 2 KB
+
+// Output tile width kBN (MMA N): 256 for large GEMMs; 128 / 64 give more tiles
+// for short-M shapes (the decoder step's M = 64) so every SM streams weights.
+// kPair: a cluster of two CTAs on one TPC computes a 256 x kBN tile with
+// tcgen05 cta_group::2 MMAs; each CTA loads its own 128 A rows and half of the
+// kBN weight rows, so per-SM operand traffic (L2 and shared memory) is a third
+// lower than one CTA computing 128 x kBN.
+template <int kBN, bool kPair = false>
+struct Tile {
+  static constexpr int B_ROWS = kPair ? kBN / 2 : kBN;  // weight rows this CTA loads per stage
+  static constexpr int B_STAGE_BYTES = B_ROWS * BK;     // 32 / 16 / 8 KB (16 KB per CTA in a pair)
+  // Shared-memory ring depth: ~192 KB of operands in flight per SM whatever the shape.
+  static constexpr int STAGES = (192 * 1024) / (A_STAGE_BYTES + B_STAGE_BYTES);
+  static constexpr int TMEM_COLS = NUM_ACC * kBN;    // 512 / 256 / 128 (power of two >= 32)
+  static constexpr int EPI_COLS = kBN / 2;           // columns per epilogue warp (two warps per lane quarter)
+  static constexpr int ROWS = kPair ? 2 * BM : BM;   // output rows per (pair) tile
+  static_assert(kBN == 64 || kBN == 128 || kBN == 256, "tile width");
+  static_assert(!kPair || kBN == 256, "CTA pairs use 256-wide tiles");
+};
 
 enum : uint32_t {
   SITE_PRODUCER_EMPTY = 1,
@@ -70,21 +84,24 @@ enum : uint32_t {
   SITE_SELFTEST = 15,
 };
 
+template <int kBN, bool kPair = false>
 struct SharedStorage {
-  uint8_t a[STAGES][A_STAGE_BYTES];  // 1024-byte aligned (swizzle atom)
-  uint8_t b[STAGES][B_STAGE_BYTES];
+  uint8_t a[Tile<kBN, kPair>::STAGES][A_STAGE_BYTES];  // 1024-byte aligned (swizzle atom)
+  uint8_t b[Tile<kBN, kPair>::STAGES][Tile<kBN, kPair>::B_STAGE_BYTES];
   uint8_t out[EPI_WARPS][2][STAGE_OUT_BYTES];  // per-warp double-buffered store staging
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[Tile<kBN, kPair>::STAGES];
+  uint64_t empty[Tile<kBN, kPair>::STAGES];
   uint64_t acc_full[NUM_ACC];
   uint64_t acc_empty[NUM_ACC];
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
 };
-constexpr size_t SMEM_BYTES = sizeof(SharedStorage) + 1024;
-static_assert(SMEM_BYTES <= 232448, "shared memory budget");
-static_assert(EPI_COLS / CHUNK == 4, "the epilogue drain below is unrolled for 4 chunks per warp");
+template <int kBN, bool kPair = false>
+constexpr size_t smem_bytes() { return sizeof(SharedStorage<kBN, kPair>) + 1024; }
+static_assert(smem_bytes<256>() <= 232448 && smem_bytes<128>() <= 232448 && smem_bytes<64>() <= 232448 &&
+                  smem_bytes<256, true>() <= 232448,
+              "shared memory budget");
 
 struct Params {
   int M, N, K;
@@ -97,6 +114,7 @@ struct Params {
   __half* out;
   uint32_t* out_amax;
   int out_pairs;  // direct-store path: rows 4-byte aligned, store fp16 pairs
+  uint32_t a_box_bytes;  // bytes one A box load delivers (64 or 128 rows x 128 B)
   uint32_t idesc;
   uint64_t timeout_ns;
 };
@@ -124,7 +142,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(parity)
@@ -226,6 +244,78 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
                : "memory");
 }
 
+// ---- CTA-pair (cta_group::2) forms
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t num_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA load into this CTA's shared memory whose bytes complete on an mbarrier in
+// either CTA of the pair (here: the leader's). No multicast.
+__device__ __forceinline__ void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster_addr, void* dst, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem of both CTAs] (+)= A[256 rows: 128 per CTA] . B[256 cols: 128 per CTA]^T, issued by the leader.
+__device__ __forceinline__ void umma_f8f6f4_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  const uint32_t z = 0;  // no disabled output lanes
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z)
+      : "memory");
+}
+// Arrive on the barrier at this offset in every CTA of `mask` once the leader's MMAs are done.
+__device__ __forceinline__ void umma_commit_pair_mc(uint64_t* bar, uint16_t mask) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+                   smem_u32(bar)),
+               "h"(mask)
+               : "memory");
+}
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns: thread i gets lane (base+i).
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -287,19 +377,20 @@ __device__ __forceinline__ void add_halves8(float* v, const uint4& raw) {
   }
 }
 
-constexpr bool has_residual(int epi) { return epi == WBK_EPI_RESIDUAL || epi == WBK_EPI_RESIDUAL_CLAMP; }
+__host__ __device__ constexpr bool has_residual(int epi) { return epi == WBK_EPI_RESIDUAL || epi == WBK_EPI_RESIDUAL_CLAMP; }
 
 // Pulls this thread's 128-column residual row segment of `tile` (256 B, two
 // 128-byte lines) into L2 ahead of use.
-template <int kEpi>
-__device__ __forceinline__ void prefetch_residual_l2(const Params& p, int tile, int quarter, int col_half, int lane) {
+template <int kBN, int kEpi>
+__device__ __forceinline__ void prefetch_residual_l2(const Params& p, int tile, int tile_rows, int row_off, int quarter,
+                                                     int col_half, int lane) {
   if (!has_residual(kEpi) || tile >= p.num_tiles) return;
-  const int row = (tile / p.tiles_n) * BM + quarter * 32 + lane;
-  const int col = (tile % p.tiles_n) * BN + col_half * EPI_COLS;
+  const int row = (tile / p.tiles_n) * tile_rows + row_off + quarter * 32 + lane;
+  const int col = (tile % p.tiles_n) * kBN + col_half * Tile<kBN>::EPI_COLS;
   if (row >= p.M || col >= p.N) return;
   const __half* base = p.residual + static_cast<int64_t>(row) * p.N + col;
   asm volatile("prefetch.global.L2 [%0];" ::"l"(base));
-  if (col + 64 < p.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + 64));
+  if (Tile<kBN>::EPI_COLS > 64 && col + 64 < p.N) asm volatile("prefetch.global.L2 [%0];" ::"l"(base + 64));
 }
 
 // Issues the residual loads of one full 32-column chunk of this thread's row
@@ -398,25 +489,31 @@ __device__ __forceinline__ float absmax_valid(float m, const float* v, int valid
 
 // ------------------------------------------------------------------- kernel
 
-template <int kEpi, bool kTmaStore>
+template <int kBN, int kEpi, bool kTmaStore, bool kPair>
 __global__ void __launch_bounds__(THREADS, 1)
 fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                 const __grid_constant__ CUtensorMap tmap_out, const Params p) {
   extern __shared__ uint8_t smem_raw[];
-  SharedStorage& s =
-      *reinterpret_cast<SharedStorage*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  SharedStorage<kBN, kPair>& s =
+      *reinterpret_cast<SharedStorage<kBN, kPair>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  using TL = Tile<kBN, kPair>;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   volatile int* abort_flag = &s.abort_flag;
+  // Tiles are 128 x kBN per CTA, or 256 x kBN per CTA pair (rank r owns rows 128r..).
+  const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+  const int first_tile = kPair ? static_cast<int>(cluster_id_x()) : static_cast<int>(blockIdx.x);
+  const int tile_stride = kPair ? static_cast<int>(num_clusters_x()) : static_cast<int>(gridDim.x);
+  const int row_off = static_cast<int>(rank) * BM;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
+    for (int i = 0; i < TL::STAGES; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
     for (int i = 0; i < NUM_ACC; ++i) {
       mbar_init(&s.acc_full[i], 1);
-      mbar_init(&s.acc_empty[i], EPI_WARPS);  // one arrival per epilogue warp
+      mbar_init(&s.acc_empty[i], kPair ? 2 * EPI_WARPS : EPI_WARPS);  // one arrival per epilogue warp (of the pair)
     }
     mbar_init(&s.drain, 1);
     s.abort_flag = 0;
@@ -426,11 +523,17 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     if (kTmaStore) prefetch_tmap(&tmap_out);
   }
   if (warp == 1) {
-    tmem_alloc(&s.tmem_base, TMEM_COLS);
-    tmem_relinquish();
+    if (kPair) {
+      tmem_alloc_pair(&s.tmem_base, TL::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(&s.tmem_base, TL::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if (kPair) cluster_sync();  // the leader's barriers are initialised before the peer signals them
   tc_fence_after();
   const uint32_t tmem_base = s.tmem_base;
 
@@ -440,18 +543,26 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile / p.tiles_n) * BM;
-        const int n0 = (tile % p.tiles_n) * BN;
+      for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_stride) {
+        const int m0 = (tile / p.tiles_n) * TL::ROWS + row_off;
+        const int n0 = (tile % p.tiles_n) * kBN + static_cast<int>(rank) * TL::B_ROWS;
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) {
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&s.full[stage], A_STAGE_BYTES + B_STAGE_BYTES);
-          tma_load_2d(&tmap_a, &s.full[stage], s.a[stage], kb * BK, m0);
-          tma_load_2d(&tmap_w, &s.full[stage], s.b[stage], kb * BK, n0);
-          if (++stage == STAGES) {
+          if (kPair) {
+            // Both CTAs' loads complete on the leader's full barrier, which expects both halves.
+            if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * (p.a_box_bytes + TL::B_STAGE_BYTES));
+            const uint32_t full_leader = mapa_shared(&s.full[stage], 0);
+            tma_load_2d_pair(&tmap_a, full_leader, s.a[stage], kb * BK, m0);
+            tma_load_2d_pair(&tmap_w, full_leader, s.b[stage], kb * BK, n0);
+          } else {
+            mbar_arrive_expect_tx(&s.full[stage], p.a_box_bytes + TL::B_STAGE_BYTES);
+            tma_load_2d(&tmap_a, &s.full[stage], s.a[stage], kb * BK, m0);
+            tma_load_2d(&tmap_w, &s.full[stage], s.b[stage], kb * BK, n0);
+          }
+          if (++stage == TL::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
@@ -461,9 +572,9 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         // Producer tail: wait until the MMA warp has released every stage, so
         // no tcgen05.commit arrival to this CTA's barriers is still in flight
         // when it exits.
-        for (int i = 0; i < STAGES; ++i) {
+        for (int i = 0; i < TL::STAGES; ++i) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) break;
-          if (++stage == STAGES) {
+          if (++stage == TL::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
@@ -471,7 +582,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       } else {
         // Abort path: let the copies already issued land before the CTA exits.
         // Stage i was last filled with phase (phase if i < stage else phase^1).
-        for (int i = 0; i < STAGES; ++i) {
+        for (int i = 0; i < TL::STAGES && (!kPair || rank == 0); ++i) {
           const uint32_t ph = (i < stage) ? phase : (phase ^ 1u);
           int dummy = 0;
           mbar_wait(&s.full[i], ph, &dummy, 1000000ull, SITE_DRAIN);
@@ -480,19 +591,19 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && (!kPair || rank == 0)) {
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_stride) {
         if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1u, abort_flag, p.timeout_ns, SITE_MMA_ACC_EMPTY)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
         for (int kb = 0; kb < p.kblocks; ++kb) {
           if (!mbar_wait(&s.full[stage], phase, abort_flag, p.timeout_ns, SITE_MMA_FULL)) {
             ok = false;
@@ -505,16 +616,23 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
           for (int k = 0; k < BK / UMMA_K; ++k) {
             // Advance the start address by k*32 bytes inside the 128-byte swizzle row.
             const uint64_t koff = static_cast<uint64_t>((k * UMMA_K) >> 4);
-            umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            if (kPair)
+              umma_f8f6f4_pair(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            else
+              umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
           }
-          umma_commit(&s.empty[stage]);  // frees this smem stage once its MMAs retire
-          if (++stage == STAGES) {
+          // frees this smem stage (in both CTAs of a pair) once its MMAs retire
+          if (kPair) umma_commit_pair_mc(&s.empty[stage], 0x3);
+          else umma_commit(&s.empty[stage]);
+          if (++stage == TL::STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&s.acc_full[acc]);  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue (of both CTAs of a pair)
+        if (kPair) umma_commit_pair_mc(&s.acc_full[acc], 0x3);
+        else umma_commit(&s.acc_full[acc]);
         if (++acc == NUM_ACC) {
           acc = 0;
           acc_phase ^= 1u;
@@ -522,7 +640,8 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       }
       if (!ok) {
         // Abort path: wait for every MMA this thread issued before TMEM is freed.
-        umma_commit(&s.drain);
+        if (kPair) umma_commit_pair(&s.drain);
+        else umma_commit(&s.drain);
         int dummy = 0;
         mbar_wait(&s.drain, 0, &dummy, 1000000ull, SITE_DRAIN);
       }
@@ -538,11 +657,11 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;  // staging buffer toggle (kTmaStore)
-    prefetch_residual_l2<kEpi>(p, blockIdx.x, quarter, col_half, lane);
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-      prefetch_residual_l2<kEpi>(p, tile + gridDim.x, quarter, col_half, lane);  // next tile of this CTA
-      const int m0 = (tile / p.tiles_n) * BM;
-      const int n0 = (tile % p.tiles_n) * BN + col_half * EPI_COLS;
+    prefetch_residual_l2<kBN, kEpi>(p, first_tile, TL::ROWS, row_off, quarter, col_half, lane);
+    for (int tile = first_tile; tile < p.num_tiles; tile += tile_stride) {
+      prefetch_residual_l2<kBN, kEpi>(p, tile + tile_stride, TL::ROWS, row_off, quarter, col_half, lane);  // next tile
+      const int m0 = (tile / p.tiles_n) * TL::ROWS + row_off;
+      const int n0 = (tile % p.tiles_n) * kBN + col_half * TL::EPI_COLS;
       const int row0 = m0 + quarter * 32;
       const int row = row0 + lane;
       uint4 resa[4], resb[4];
@@ -550,8 +669,8 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       if (!mbar_wait(&s.acc_full[acc], acc_phase, abort_flag, p.timeout_ns, SITE_EPI_ACC_FULL)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                             static_cast<uint32_t>(acc * BN + col_half * EPI_COLS);
-      const int nchunks = min(EPI_COLS / CHUNK, (p.N - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
+                             static_cast<uint32_t>(acc * kBN + col_half * TL::EPI_COLS);
+      const int nchunks = min(TL::EPI_COLS / CHUNK, (p.N - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
       auto process = [&](const uint32_t* regs, const uint4* res, int c) {
         const int col0 = n0 + c * CHUNK;
         float v[32];
@@ -621,7 +740,10 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.acc_empty[acc]);
+      if (lane == 0) {
+        if (kPair && rank != 0) mbar_arrive_remote(mapa_shared(&s.acc_empty[acc], 0));  // the leader's barrier
+        else mbar_arrive(&s.acc_empty[acc]);
+      }
       if (++acc == NUM_ACC) {
         acc = 0;
         acc_phase ^= 1u;
@@ -637,9 +759,11 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
 
   tc_fence_before();
   __syncthreads();
+  if (kPair) cluster_sync();  // neither CTA leaves while its pair may still touch its shared memory or TMEM
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (kPair) tmem_dealloc_pair(tmem_base, TL::TMEM_COLS);
+    else tmem_dealloc(tmem_base, TL::TMEM_COLS);
   }
 }
 
@@ -696,33 +820,105 @@ uint64_t wait_timeout_ns() {
   return t;
 }
 
-template <int kEpi, bool kTma>
+template <int kBN, int kEpi, bool kTma, bool kPair>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const Params& p, int grid,
                 cudaStream_t stream) {
   static std::mutex mu;
   static std::vector<char> configured;
   const int dev = current_device();
   if (dev < 0) return fail(WBK_ERR_CUDA, "no current CUDA device");
+  constexpr size_t kSmem = smem_bytes<kBN, kPair>();
+  auto kernel = fp8_gemm_kernel<kBN, kEpi, kTma, kPair>;
   {
     std::lock_guard<std::mutex> lock(mu);
     if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
     if (!configured[dev]) {
-      if (int e = cuda_check(cudaFuncSetAttribute(fp8_gemm_kernel<kEpi, kTma>,
-                                                  cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  static_cast<int>(SMEM_BYTES)),
+      if (int e = cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(kSmem)),
                              "cudaFuncSetAttribute(max dynamic smem)"))
         return e;
       configured[dev] = 1;
     }
   }
-  fp8_gemm_kernel<kEpi, kTma><<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tw, to, p);
-  return cuda_check(cudaGetLastError(), "fp8 gemm launch");
+  if (!kPair) {
+    kernel<<<grid, THREADS, kSmem, stream>>>(ta, tw, to, p);
+    return cuda_check(cudaGetLastError(), "fp8 gemm launch");
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  {
+    // Persistent pairs: never launch more clusters than can be resident at once.
+    static std::vector<int> max_clusters;
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(max_clusters.size()) <= dev) max_clusters.resize(dev + 1, -1);
+    if (max_clusters[dev] < 0) {
+      cudaLaunchConfig_t q = {};
+      q.gridDim = cfg.gridDim;
+      q.blockDim = dim3(THREADS, 1, 1);
+      q.dynamicSmemBytes = kSmem;
+      cudaLaunchAttribute qa[1];
+      qa[0].id = cudaLaunchAttributeClusterDimension;
+      qa[0].val.clusterDim.x = 2;
+      qa[0].val.clusterDim.y = 1;
+      qa[0].val.clusterDim.z = 1;
+      q.attrs = qa;
+      q.numAttrs = 1;
+      int n = 0;
+      if (int e = cuda_check(cudaOccupancyMaxActiveClusters(&n, kernel, &q), "cudaOccupancyMaxActiveClusters"))
+        return e;
+      if (n < 1) return fail(WBK_ERR_UNSUPPORTED, "fp8 gemm: no CTA pair fits on this device");
+      max_clusters[dev] = n;
+    }
+    if (grid > 2 * max_clusters[dev]) cfg.gridDim.x = static_cast<unsigned>(2 * max_clusters[dev]);
+  }
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, p), "fp8 gemm (CTA pair) launch");
 }
 
-template <int kEpi>
+template <int kBN, int kEpi, bool kPair>
 int dispatch_store(bool tma, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const Params& p,
                    int grid, cudaStream_t s) {
-  return tma ? launch_gemm<kEpi, true>(ta, tw, to, p, grid, s) : launch_gemm<kEpi, false>(ta, tw, to, p, grid, s);
+  return tma ? launch_gemm<kBN, kEpi, true, kPair>(ta, tw, to, p, grid, s)
+             : launch_gemm<kBN, kEpi, false, kPair>(ta, tw, to, p, grid, s);
+}
+
+template <int kBN, bool kPair = false>
+int dispatch_epi(int epilogue, bool tma, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to,
+                 const Params& p, int grid, cudaStream_t s) {
+  switch (epilogue) {
+    case WBK_EPI_NONE: return dispatch_store<kBN, WBK_EPI_NONE, kPair>(tma, ta, tw, to, p, grid, s);
+    case WBK_EPI_GELU: return dispatch_store<kBN, WBK_EPI_GELU, kPair>(tma, ta, tw, to, p, grid, s);
+    case WBK_EPI_RESIDUAL: return dispatch_store<kBN, WBK_EPI_RESIDUAL, kPair>(tma, ta, tw, to, p, grid, s);
+    case WBK_EPI_RESIDUAL_CLAMP:
+      return dispatch_store<kBN, WBK_EPI_RESIDUAL_CLAMP, kPair>(tma, ta, tw, to, p, grid, s);
+    default: return dispatch_store<kBN, WBK_EPI_BIAS_MAXKEY, kPair>(tma, ta, tw, to, p, grid, s);
+  }
+}
+
+bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Tile width: 256 unless that leaves SMs idle. Short-M GEMMs (the decoder step)
+// are weight-streaming, HBM-bound: narrow tiles spread the weight over every SM.
+int pick_bn(int64_t M, int64_t N, int sms) {
+  const int64_t tiles_m = (M + BM - 1) / BM;
+  if (M <= BM) return 64;
+  if (tiles_m * ((N + 255) / 256) >= 2 * sms) return 256;
+  return 128;
 }
 
 }  // namespace
@@ -759,8 +955,18 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, 
   const bool vec = (N % 8 == 0) && aligned(out, 16) && (!bias || aligned(bias, 16)) && (!residual || aligned(residual, 16));
 
   CUtensorMap ta, tw, to;
-  if (int e = make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, BK, BM, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
-  if (int e = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, K, N, BK, BN, CU_TENSOR_MAP_SWIZZLE_128B)) return e;
+  // M <= 64 (decoder step): load a 64-row A box; the MMA still reads 128 rows, and
+  // TMEM lanes 64..127 (computed from stale shared memory) are never stored.
+  const uint32_t a_box_rows = M <= 64 ? 64u : static_cast<uint32_t>(BM);
+  if (int e = make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, BK, a_box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int bn = pick_bn(M, N, sms);
+  // Large GEMMs run on CTA pairs (256 x 256 tiles, each CTA loading half of the weight rows).
+  const bool pair = bn == 256 && pair_enabled() && sms >= 2;
+  const uint32_t w_box_rows = static_cast<uint32_t>(pair ? bn / 2 : bn);
+  if (int e = make_tmap(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, K, N, BK, w_box_rows, CU_TENSOR_MAP_SWIZZLE_128B))
+    return e;
   if (vec) {
     if (int e = make_tmap(&to, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, out, N, M, CHUNK, 32, CU_TENSOR_MAP_SWIZZLE_64B))
       return e;
@@ -772,8 +978,9 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, 
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
-  const int tiles_m = static_cast<int>((M + BM - 1) / BM);
-  p.tiles_n = static_cast<int>((N + BN - 1) / BN);
+  const int tile_rows = pair ? 2 * BM : BM;
+  const int tiles_m = static_cast<int>((M + tile_rows - 1) / tile_rows);
+  p.tiles_n = static_cast<int>((N + bn - 1) / bn);
   const int64_t num_tiles = static_cast<int64_t>(tiles_m) * p.tiles_n;
   if (num_tiles > INT32_MAX) return fail(WBK_ERR_UNSUPPORTED, "wbk_gemm_fp8: too many tiles");
   p.num_tiles = static_cast<int>(num_tiles);
@@ -786,22 +993,23 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, 
   p.out = static_cast<__half*>(out);
   p.out_amax = out_amax_bits;
   p.out_pairs = (N % 2 == 0) && aligned(out, 4);
+  p.a_box_bytes = a_box_rows * BK;
   // Instruction descriptor (kind::f8f6f4): D fp32 [4,6)=1; A format [7,10);
   // B format [10,13); both K-major (bits 15,16 = 0); N>>3 [17,23); M>>4 [24,29).
   p.idesc = (1u << 4) | (static_cast<uint32_t>(a_fmt) << 7) | (static_cast<uint32_t>(w_fmt) << 10) |
-            (static_cast<uint32_t>(BN >> 3) << 17) | (static_cast<uint32_t>(BM >> 4) << 24);
+            (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(tile_rows >> 4) << 24);
   p.timeout_ns = wait_timeout_ns();
 
-  const int sms = sm_count() > 0 ? sm_count() : 148;
-  const int grid = static_cast<int>(num_tiles < sms ? num_tiles : sms);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  switch (epilogue) {
-    case WBK_EPI_NONE: return dispatch_store<WBK_EPI_NONE>(vec, ta, tw, to, p, grid, s);
-    case WBK_EPI_GELU: return dispatch_store<WBK_EPI_GELU>(vec, ta, tw, to, p, grid, s);
-    case WBK_EPI_RESIDUAL: return dispatch_store<WBK_EPI_RESIDUAL>(vec, ta, tw, to, p, grid, s);
-    case WBK_EPI_RESIDUAL_CLAMP: return dispatch_store<WBK_EPI_RESIDUAL_CLAMP>(vec, ta, tw, to, p, grid, s);
-    default: return dispatch_store<WBK_EPI_BIAS_MAXKEY>(vec, ta, tw, to, p, grid, s);
+  if (pair) {
+    const int pairs = sms / 2;
+    const int grid = 2 * static_cast<int>(num_tiles < pairs ? num_tiles : pairs);
+    return dispatch_epi<256, true>(epilogue, vec, ta, tw, to, p, grid, s);
   }
+  const int grid = static_cast<int>(num_tiles < sms ? num_tiles : sms);
+  if (bn == 64) return dispatch_epi<64>(epilogue, vec, ta, tw, to, p, grid, s);
+  if (bn == 128) return dispatch_epi<128>(epilogue, vec, ta, tw, to, p, grid, s);
+  return dispatch_epi<256>(epilogue, vec, ta, tw, to, p, grid, s);
 }
 
 int wbk_device_error(uint32_t* code_out) {

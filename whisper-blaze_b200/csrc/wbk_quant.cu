@@ -304,6 +304,58 @@ int launch_quantise_gelu(const __half* y, int64_t n, const uint32_t* amax, float
   return cuda_check(cudaGetLastError(), "wbk_quantise_gelu_f16 launch");
 }
 
+// ------------------------------------------------- small-tensor quantise
+//
+// For small tensors (the decoder step's 64 x 1280 activation) three launches
+// (memset, amax, quantise) cost more than the data movement. One CTA does all
+// of it: amax, the scale, then the quantise pass over the (now L1/L2 resident)
+// input — the same scale rule and element rule as the two-kernel path.
+constexpr int kSmallThreads = 1024;
+constexpr int64_t kSmallQuantMax = 262144;  // elements (512 KB of fp16)
+
+template <int kFmt, bool kVec>
+__global__ void __launch_bounds__(kSmallThreads, 1)
+quantise_small_kernel(const __half* __restrict__ x, int64_t n, float max_fp8, uint8_t* __restrict__ q,
+                      float* __restrict__ scale_out, uint32_t* __restrict__ amax_out) {
+  __shared__ uint32_t red[kSmallThreads / 32];
+  __shared__ float sc[2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t nvec = kVec ? (n >> 3) : 0;
+  uint32_t m = 0;
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  for (int64_t i = threadIdx.x; i < nvec; i += kSmallThreads) {
+    const uint4 v = xv[i];
+    m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v.x), abs2_nonan(v.y)), __vmaxu2(abs2_nonan(v.z), abs2_nonan(v.w))));
+  }
+  const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
+  for (int64_t i = (nvec << 3) + threadIdx.x; i < n; i += kSmallThreads) m = __vmaxu2(m, abs2_nonan(xs[i]));
+  uint32_t mm = warp_max_u32(max(m & 0xFFFFu, m >> 16));
+  if (lane == 0) red[warp] = mm;
+  __syncthreads();
+  if (warp == 0) {
+    mm = warp_max_u32(red[lane]);
+    if (lane == 0) {
+      float scale, inv;
+      scale_from_amax(mm, max_fp8, scale, inv);
+      sc[0] = scale;
+      sc[1] = inv;
+      if (scale_out != nullptr) *scale_out = scale;
+      if (amax_out != nullptr) *amax_out = mm;
+    }
+  }
+  __syncthreads();
+  const float inv = sc[1];
+  uint2* qv = reinterpret_cast<uint2*>(q);
+  for (int64_t i = threadIdx.x; i < nvec; i += kSmallThreads) {
+    const uint4 v = xv[i];
+    qv[i] = make_uint2(q8x4<kFmt>(v.x, v.y, inv, max_fp8), q8x4<kFmt>(v.z, v.w, inv, max_fp8));
+  }
+  for (int64_t i = (nvec << 3) + threadIdx.x; i < n; i += kSmallThreads) {
+    const float f = __half2float(x[i]);
+    q[i] = static_cast<uint8_t>(q8x2<kFmt>(f, 0.0f, inv, max_fp8) & 0xFFu);
+  }
+}
+
 // -------------------------------------------------------------- dequantise
 
 template <int kFmt>
@@ -487,6 +539,20 @@ int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out, float* scal
   if (n < 0) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_f16: n < 0");
   if (n > 0 && (x == nullptr || q_out == nullptr)) return fail(WBK_ERR_INVALID_ARG, "wbk_quantise_f16: null pointer");
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (n <= kSmallQuantMax) {  // one launch; *amax_ws receives the amax as in the general path
+    const bool vec = aligned(x, 16) && aligned(q_out, 8);
+    const __half* xh = static_cast<const __half*>(x);
+    uint8_t* q = static_cast<uint8_t*>(q_out);
+    const float mx = fmt_max(fmt);
+    if (fmt == WBK_FMT_E4M3) {
+      if (vec) quantise_small_kernel<WBK_FMT_E4M3, true><<<1, kSmallThreads, 0, s>>>(xh, n, mx, q, scale_out, amax_ws);
+      else quantise_small_kernel<WBK_FMT_E4M3, false><<<1, kSmallThreads, 0, s>>>(xh, n, mx, q, scale_out, amax_ws);
+    } else {
+      if (vec) quantise_small_kernel<WBK_FMT_E5M2, true><<<1, kSmallThreads, 0, s>>>(xh, n, mx, q, scale_out, amax_ws);
+      else quantise_small_kernel<WBK_FMT_E5M2, false><<<1, kSmallThreads, 0, s>>>(xh, n, mx, q, scale_out, amax_ws);
+    }
+    return cuda_check(cudaGetLastError(), "wbk_quantise_f16 (small) launch");
+  }
   if (int e = cuda_check(cudaMemsetAsync(amax_ws, 0, sizeof(uint32_t), s), "wbk_quantise_f16 memset")) return e;
   if (int e = wbk_amax_f16(x, n, amax_ws, stream)) return e;
   return wbk_quantise_from_amax_f16(x, n, fmt, amax_ws, q_out, scale_out, stream);
