@@ -62,29 +62,39 @@ __device__ __forceinline__ void block_amax_commit(uint32_t m, uint32_t* out_amax
 // Per-row pieces shared by every mode of norm_warp_kernel, so the stats-only
 // pass and the quantise pass of the fused LayerNorm->FP8 path compute exactly
 // the same fp16 outputs as the plain LayerNorm.
-template <int kVpl>
-__device__ __forceinline__ void load_row(const uint4* xr, const uint4* rr, int lane, int nvec, float (&v)[kVpl][8]) {
+// kRes = false: the residual operand is known to be absent at compile time and
+// its registers are not allocated.
+template <int kVpl, bool kRes>
+__device__ __forceinline__ void load_row_raw(const uint4* xr, const uint4* rr, int lane, int nvec, uint4 (&xv)[kVpl],
+                                             uint4 (&rv)[kVpl]) {
 #pragma unroll
   for (int i = 0; i < kVpl; ++i) {
     const int idx = lane + 32 * i;
-    if (idx < nvec) {
-      unpack8(ld_stream16(xr + idx), v[i]);
-      if (rr) {
-        float r8[8];
-        unpack8(ld_stream16(rr + idx), r8);
+    xv[i] = idx < nvec ? ld_stream16(xr + idx) : make_uint4(0, 0, 0, 0);
+    if (kRes && rr) rv[i] = idx < nvec ? ld_stream16(rr + idx) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <int kVpl, bool kRes>
+__device__ __forceinline__ void unpack_row(const uint4 (&xv)[kVpl], const uint4 (&rv)[kVpl], bool has_res,
+                                           float (&v)[kVpl][8]) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] += r8[j];
-      }
-    } else {
+  for (int i = 0; i < kVpl; ++i) {
+    unpack8(xv[i], v[i]);
+    if (kRes && has_res) {
+      float r8[8];
+      unpack8(rv[i], r8);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[i][j] = 0.0f;
+      for (int j = 0; j < 8; ++j) v[i][j] += r8[j];
     }
   }
 }
 
+// Row statistics. LayerNorm leaves v[i][j] - mean in v (the same fp32 value
+// the normalisation subtracts), so normalise8 takes centred values.
 template <int kVpl, bool kRms>
-__device__ __forceinline__ void row_stats(const float (&v)[kVpl][8], int lane, int nvec, float fD, float eps,
-                                          float& mean, float& inv) {
+__device__ __forceinline__ void row_stats(float (&v)[kVpl][8], int lane, int nvec, float fD, float eps, float& mean,
+                                          float& inv) {
   float s = 0.0f;
 #pragma unroll
   for (int i = 0; i < kVpl; ++i)
@@ -100,33 +110,42 @@ __device__ __forceinline__ void row_stats(const float (&v)[kVpl][8], int lane, i
   float var = 0.0f;
 #pragma unroll
   for (int i = 0; i < kVpl; ++i) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[i][j] -= mean;
     if (lane + 32 * i < nvec) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float d = v[i][j] - mean;
-        var += d * d;
-      }
+      for (int j = 0; j < 8; ++j) var += v[i][j] * v[i][j];
     }
   }
   var = warp_sum(var);
   inv = rsqrtf(var / fD + eps);
 }
 
+// fp32 outputs before the fp16 rounding: LayerNorm fma(d * inv, gamma, beta)
+// with d = s - mean, RMSNorm (s * inv) * gamma.
 template <bool kRms>
-__device__ __forceinline__ uint4 normalise8(const float* v8, int idx, const __half* __restrict__ gamma,
-                                            const __half* __restrict__ beta, float mean, float inv) {
-  float g[8], o[8];
+__device__ __forceinline__ void normalise8(const float* d8, int idx, const __half* __restrict__ gamma,
+                                           const __half* __restrict__ beta, float inv, float* o) {
+  float g[8];
   unpack8(__ldg(reinterpret_cast<const uint4*>(gamma) + idx), g);
   if (kRms) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = (v8[j] * inv) * g[j];
+    for (int j = 0; j < 8; ++j) o[j] = (d8[j] * inv) * g[j];
   } else {
     float b[8];
     unpack8(__ldg(reinterpret_cast<const uint4*>(beta) + idx), b);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = fmaf((v8[j] - mean) * inv, g[j], b[j]);
+    for (int j = 0; j < 8; ++j) o[j] = fmaf(d8[j] * inv, g[j], b[j]);
   }
-  return pack8(o);
+}
+
+// max |o| over 8 fp32 outputs; NaN is skipped (fmaxf), as abs2_nonan skips it
+// in the fp16 amax. Rounding to fp16 is monotone and symmetric, so
+// fp16(max|o|) equals the max of |fp16(o)|: the amax of the stored outputs.
+__device__ __forceinline__ float absmax8(const float* o, float m) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(o[j]));
+  return m;
 }
 
 enum NormMode { kModeNormal = 0, kModeStats = 1, kModeQuant = 2 };
@@ -135,8 +154,10 @@ enum NormMode { kModeNormal = 0, kModeStats = 1, kModeQuant = 2 };
 //   kModeNormal: out (+ sum_out, + out_amax) as wbk_layernorm_f16 / wbk_rmsnorm_f16;
 //   kModeStats:  stats[row] = (mean, rstd) and out_amax of the fp16 outputs, nothing else stored;
 //   kModeQuant:  fp8 codes of the fp16 outputs, from stats[] and scale_inv = (scale, 1/scale).
+// Rows up to 1536 wide (kVpl <= 6) run two CTAs per SM; without a residual
+// operand they are also software-pipelined (two rows in flight per warp).
 template <int kVpl, bool kRms, int kMode, int kFmt>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, kVpl <= 6 ? 2 : 1)
 norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, const __half* __restrict__ gamma,
                  const __half* __restrict__ beta, __half* __restrict__ out, __half* __restrict__ sum_out,
                  int64_t rows, int D, float eps, uint32_t* __restrict__ out_amax, float2* __restrict__ stats,
@@ -144,24 +165,33 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = D >> 3;
   const float fD = static_cast<float>(D);
-  uint32_t amax = 0;
+  float amax_f = 0.0f;
   float qinv = 0.0f;
   constexpr float kMx = kFmt == WBK_FMT_E4M3 ? 448.0f : 57344.0f;
   if (kMode == kModeQuant) {
     qinv = scale_inv[1];
     if (scale_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale_inv[0];
   }
-  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp; row < rows;
-       row += static_cast<int64_t>(gridDim.x) * kWarps) {
-    const uint4* xr = reinterpret_cast<const uint4*>(x + row * D);
-    const uint4* rr = res ? reinterpret_cast<const uint4*>(res + row * D) : nullptr;
+  // Rows are software-pipelined: the loads of this warp's next row are issued
+  // before the current row's reductions, so each warp keeps a row in flight.
+  constexpr bool kRes = kMode == kModeNormal;  // the fused LayerNorm->FP8 passes take no residual
+  auto process_row = [&](int64_t row, const uint4 (&xv)[kVpl], const uint4 (&rv)[kVpl]) {
     float v[kVpl][8];
-    load_row<kVpl>(xr, rr, lane, nvec, v);
+    unpack_row<kVpl, kRes>(xv, rv, res != nullptr, v);
+    if (kMode == kModeNormal && sum_out) {  // fp16(s), before LayerNorm centres v
+#pragma unroll
+      for (int i = 0; i < kVpl; ++i)
+        if (lane + 32 * i < nvec) reinterpret_cast<uint4*>(sum_out + row * D)[lane + 32 * i] = pack8(v[i]);
+    }
     float mean, inv;
     if (kMode == kModeQuant) {
       const float2 st = stats[row];
       mean = st.x;
       inv = st.y;
+#pragma unroll
+      for (int i = 0; i < kVpl; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] -= mean;
     } else {
       row_stats<kVpl, kRms>(v, lane, nvec, fD, eps, mean, inv);
       if (kMode == kModeStats && lane == 0) stats[row] = make_float2(mean, inv);
@@ -170,24 +200,23 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
     for (int i = 0; i < kVpl; ++i) {
       const int idx = lane + 32 * i;
       if (idx < nvec) {
-        const uint4 ov = normalise8<kRms>(v[i], idx, gamma, beta, mean, inv);
-        if (kMode == kModeNormal) {
-          reinterpret_cast<uint4*>(out + row * D)[idx] = ov;
-          if (sum_out) reinterpret_cast<uint4*>(sum_out + row * D)[idx] = pack8(v[i]);
-        }
-        if (kMode != kModeQuant && out_amax) amax = max(amax, amax8(ov));
+        float o[8];
+        normalise8<kRms>(v[i], idx, gamma, beta, inv, o);
+        if (kMode != kModeQuant && out_amax) amax_f = absmax8(o, amax_f);
+        if (kMode == kModeNormal) reinterpret_cast<uint4*>(out + row * D)[idx] = pack8(o);
         if (kMode == kModeQuant) {
-          const uint32_t w[4] = {ov.x, ov.y, ov.z, ov.w};
+          // fp8(fp16(o) * (1/scale)): fmaxf maps NaN to -max as the quantiser's
+          // clamp does; satfinite clamps everything else to +-max.
           uint32_t q[2];
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * t]));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * t + 1]));
+            const float2 f0 = __half22float2(__floats2half2_rn(o[4 * t], o[4 * t + 1]));
+            const float2 f1 = __half22float2(__floats2half2_rn(o[4 * t + 2], o[4 * t + 3]));
             float2 c0, c1;
-            c0.x = fminf(fmaxf(f0.x * qinv, -kMx), kMx);
-            c0.y = fminf(fmaxf(f0.y * qinv, -kMx), kMx);
-            c1.x = fminf(fmaxf(f1.x * qinv, -kMx), kMx);
-            c1.y = fminf(fmaxf(f1.y * qinv, -kMx), kMx);
+            c0.x = fmaxf(f0.x * qinv, -kMx);
+            c0.y = fmaxf(f0.y * qinv, -kMx);
+            c1.x = fmaxf(f1.x * qinv, -kMx);
+            c1.y = fmaxf(f1.y * qinv, -kMx);
             const __nv_fp8_interpretation_t it = kFmt == WBK_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2;
             q[t] = static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(c0, __NV_SATFINITE, it)) |
                    (static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(c1, __NV_SATFINITE, it)) << 16);
@@ -196,8 +225,65 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
         }
       }
     }
+  };
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
+  int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  auto row_ptrs = [&](int64_t r, const uint4*& xr, const uint4*& rr) {
+    xr = reinterpret_cast<const uint4*>(x + r * D);
+    rr = res ? reinterpret_cast<const uint4*>(res + r * D) : nullptr;
+  };
+  uint4 xa[kVpl], ra[kVpl], xb[kVpl], rb[kVpl];
+  const uint4 *xr, *rr;
+  if (kVpl > 6 || (kRes && res != nullptr)) {  // one row in flight per warp
+    for (; row < rows; row += stride) {
+      row_ptrs(row, xr, rr);
+      load_row_raw<kVpl, kRes>(xr, rr, lane, nvec, xa, ra);
+      process_row(row, xa, ra);
+    }
+  } else {
+    if (row < rows) {
+      row_ptrs(row, xr, rr);
+      load_row_raw<kVpl, kRes>(xr, rr, lane, nvec, xa, ra);
+    }
+    while (row < rows) {
+      int64_t next = row + stride;
+      if (next < rows) {
+        row_ptrs(next, xr, rr);
+        load_row_raw<kVpl, kRes>(xr, rr, lane, nvec, xb, rb);
+      }
+      process_row(row, xa, ra);
+      row = next;
+      if (row >= rows) break;
+      next = row + stride;
+      if (next < rows) {
+        row_ptrs(next, xr, rr);
+        load_row_raw<kVpl, kRes>(xr, rr, lane, nvec, xa, ra);
+      }
+      process_row(row, xb, rb);
+      row = next;
+    }
   }
-  if (kMode != kModeQuant && out_amax) block_amax_commit(amax, out_amax);
+  if (kMode != kModeQuant && out_amax)
+    block_amax_commit(static_cast<uint32_t>(__half_as_ushort(__float2half_rn(amax_f))), out_amax);
+}
+
+// One wave of norm_warp_kernel: resident CTAs per SM (from the occupancy
+// calculator, once per instantiation) x SMs, fewer when there are fewer rows.
+template <int kVpl, bool kRms, int kMode, int kFmt>
+int norm_warp_grid(int64_t rows) {
+  static const int per_sm = [] {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, norm_warp_kernel<kVpl, kRms, kMode, kFmt>, kThreads, 0) !=
+            cudaSuccess || n < 1) {
+      (void)cudaGetLastError();
+      n = 1;
+    }
+    return n;
+  }();
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t want = (rows + kWarps - 1) / kWarps;
+  const int64_t cap = static_cast<int64_t>(sms) * per_sm;
+  return static_cast<int>(want < cap ? want : cap);
 }
 
 // CTA per row, for D > 32*8*16. Three reads of the row (L2-resident).
@@ -298,10 +384,9 @@ int launch_norm(const void* x, const void* res, const void* gamma, const void* b
   const int d = static_cast<int>(D);
   const int nvec = d / 8;
   const int sms = sm_count() > 0 ? sm_count() : 148;
-  const int64_t want = (rows + kWarps - 1) / kWarps;
-  const int grid = static_cast<int>(want < sms * 4 ? want : sms * 4);
 #define WBK_NORM_CASE(V)                                                                       \
   if (nvec <= 32 * (V)) {                                                                      \
+    const int grid = norm_warp_grid<V, kRms, kModeNormal, 0>(rows);                            \
     norm_warp_kernel<V, kRms, kModeNormal, 0><<<grid, kThreads, 0, s>>>(xh, rh, gh, bh, oh, sh, rows, d, eps,  \
                                                                       out_amax, nullptr, nullptr, nullptr, nullptr); \
     return cuda_check(cudaGetLastError(), "norm kernel launch");                               \
@@ -327,11 +412,9 @@ template <int kMode, int kFmt>
 int launch_ln_mode(const __half* x, const __half* gamma, const __half* beta, int64_t rows, int D, float eps,
                    uint32_t* amax, float2* stats, const float* scale_inv, uint8_t* q, float* scale_out, cudaStream_t s) {
   const int nvec = D / 8;
-  const int sms = sm_count() > 0 ? sm_count() : 148;
-  const int64_t want = (rows + kWarps - 1) / kWarps;
-  const int grid = static_cast<int>(want < sms * 4 ? want : sms * 4);
 #define WBK_LNQ_CASE(V)                                                                                  \
   if (nvec <= 32 * (V)) {                                                                                \
+    const int grid = norm_warp_grid<V, false, kMode, kFmt>(rows);                                       \
     norm_warp_kernel<V, false, kMode, kFmt><<<grid, kThreads, 0, s>>>(x, nullptr, gamma, beta, nullptr, \
                                                                       nullptr, rows, D, eps, amax,       \
                                                                       stats, scale_inv, q, scale_out);   \
