@@ -459,13 +459,51 @@ def run_gemm_configs(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_attention(args, world, rank, local):
+    """Encoder self-attention of the stack shape: `--chunks` x 20 heads x 1500 x 64 on the
+    strided q/k/v views of a fused [T, 3840] QKV buffer, output into [T, 1280]; the tcgen05
+    kernel against torch SDPA (cuDNN) on the same views. TFLOP/s = 4 B H S^2 Dh / t."""
+    from whisper_blaze_b200 import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    B, S, H, Dh = args.chunks, 1500, 20, 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    qkv = torch.randn(B * S, 3 * H * Dh, generator=g, device=dev).half()
+    v5 = qkv.view(B, S, 3, H, Dh)
+    q, k, v = (v5[:, :, i].transpose(1, 2) for i in range(3))
+    out = torch.empty(B * S, H * Dh, dtype=torch.float16, device=dev)
+    amax = ops.new_amax_ws(dev)
+    ours = lambda: ops.attention(q, k, v, out=out.view(B, S, H, Dh).transpose(1, 2), out_amax=amax)  # noqa: E731
+    sdpa = lambda: torch.nn.functional.scaled_dot_product_attention(q, k, v)  # noqa: E731
+    flops = 4.0 * B * H * S * S * Dh
+    ms = _graph_time(ours, args.steps, args.warmup, reps=4)
+    ms_sdpa = _graph_time(sdpa, args.steps, args.warmup, reps=4)
+    peak = measured_peaks().get("bf16_tflops")
+    value = flops / ms / 1e9
+    line = {"metric": "encoder self-attention TFLOP/s (fp16, head dim 64)", "value": value, "unit": "TFLOP/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "dtype": "fp16 (fp32 softmax and accumulate)", "data": "synthetic",
+            "timing": "CUDA graph of 4 back-to-back calls, device time per call",
+            "config": {"workload": "attention", "batch": B, "heads": H, "seq_len": S, "head_dim": Dh,
+                       "layout": "strided views of a fused QKV buffer"},
+            "ms_per_call": ms, "sdpa_ms_per_call": ms_sdpa, "sdpa_tflops": flops / ms_sdpa / 1e9,
+            "roofline": {"bound": "tensor (exp throughput in practice)", "achieved": value, "peak": peak,
+                         "unit": "TFLOP/s", "frac": value / peak if peak else None,
+                         "peak_source": "bf16_tflops of MEASURED_PEAKS.json (dense fp16 = dense bf16 rate)"}}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "layer", "fc1", "decoder", "crossattn"], default="stack")
+    ap.add_argument("--workload", choices=["stack", "layer", "fc1", "decoder", "crossattn", "attention"],
+                    default="stack")
+    ap.add_argument("--chunks", type=int, default=64, help="batch of the attention workload")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--ref-step-budget", type=float, default=8.0)
@@ -480,6 +518,8 @@ def main():
             run_reference_arm(args, world, rank)
         elif args.workload == "stack":
             run_stack(args, world, rank, local)
+        elif args.workload == "attention":
+            run_attention(args, world, rank, local)
         else:
             run_gemm_configs(args, world, rank, local)
     finally:

@@ -205,6 +205,26 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K,
                  const void* bias, const void* residual, void* out,
                  int epilogue, uint32_t* out_amax_bits, wbk_stream_t stream);
 
+/* ------------------------------------------------------------ attention */
+
+/* Non-causal multi-head attention forward for head_dim 64:
+ *   out[b,h,i,:] = sum_j softmax_j(scale * q[b,h,i,:] . k[b,h,j,:]) v[b,h,j,:]
+ * fp16 q/k/v/out, fp32 scores, softmax and accumulation (tcgen05 kind::f16).
+ * Each of q, k, v, out is a [batch, heads, seq, 64] view with the 64 dims
+ * contiguous and element strides given in the HOST array
+ *   strides[12] = {q_b, q_h, q_s, k_b, k_h, k_s, v_b, v_h, v_s, o_b, o_h, o_s},
+ * each a positive multiple of 8; pointers 16-byte aligned. seq_q and seq_k may
+ * differ (cross-attention). If out_amax_bits is non-NULL, max|out| (fp16 bits,
+ * NaN ignored) is max-accumulated into it as wbk_amax_f16 does.
+ * Replaces: encoder_self_attn and decoder_cross_attn, bound at
+ * csrc/ops/bindings.cpp:152-167, 229-235 (flash_attn_forward,
+ * csrc/kernels/flash_attn_hopper.cu:297-365, scale = 1/sqrt(D), whose kernel
+ * is unfinished upstream); in the encoder stack it stands where
+ * HF WhisperAttention calls torch SDPA. */
+int wbk_attention_f16(const void* q, const void* k, const void* v, void* out,
+                      int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k, int64_t head_dim,
+                      const int64_t* strides, float scale, uint32_t* out_amax_bits, wbk_stream_t stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

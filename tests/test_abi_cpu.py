@@ -68,8 +68,13 @@ def test_python_surface_checks_before_any_launch():
         K.quantise_e4m3(x)
     with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
         K.layernorm_fused(x, None, torch.ones(16).half(), torch.zeros(16).half())
+    x4 = torch.randn(1, 2, 16, 64).half()
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        K.encoder_self_attn(x4, x4, x4)
     with pytest.raises(NotImplementedError):
-        K.encoder_self_attn(x, x, x)
+        K.decoder_self_attn(x4, x4, x4)
+    with pytest.raises(NotImplementedError):
+        K.mel_spectrogram(torch.zeros(16000))
     for name in ("quantise_e4m3", "quantise_e5m2", "dequantise_e4m3", "dequantise_e5m2", "layernorm_fused",
                  "layernorm_fused_residual", "rmsnorm_fused", "mel_spectrogram", "encoder_self_attn",
                  "decoder_cross_attn", "decoder_self_attn", "gemm_fp8_e4m3"):

@@ -1,5 +1,6 @@
 """GPU parity of the FP8 encoder stack against the CPU oracle.
 
+Both attention back ends of the stack (the tcgen05 kernel and torch SDPA) are covered.
 Stage-wise, teacher-forced: every stage of a layer is recomputed by the oracle
 from the GPU's own input to that stage and held to that stage's gate
 (LayerNorm 1e-3 abs / fp16 ulp; fp8 bytes exact for the GPU's scale, scale
@@ -46,10 +47,11 @@ def _check_gemm(y, ref32):
     assert rel <= 1e-2, f"GEMM relative error {rel:.3e}"
 
 
+@pytest.mark.parametrize("attention", ["wbk", "sdpa"])
 @pytest.mark.parametrize("B,S", [(2, 64), (1, 1500)])
-def test_layer_stagewise_parity(cuda_device, B, S):
+def test_layer_stagewise_parity(cuda_device, B, S, attention):
     cfg = EncoderConfig(layers=1, seq_len=S)
-    stack = FP8EncoderStack(cfg, _layers(cfg, 1, 5), cuda_device)
+    stack = FP8EncoderStack(cfg, _layers(cfg, 1, 5), cuda_device, attention=attention)
     L = stack.layers[0]
     h = randn_f16((B, S, cfg.d_model), 6)
     cap = []
@@ -80,10 +82,11 @@ def test_layer_stagewise_parity(cuda_device, B, S):
                                                 cpu(L.b_fc2), c["h2"], gemm.EPI_RESIDUAL_CLAMP))
 
 
-def test_two_layer_stack_statistics(cuda_device):
+@pytest.mark.parametrize("attention", ["wbk", "sdpa"])
+def test_two_layer_stack_statistics(cuda_device, attention):
     cfg = EncoderConfig(layers=2, seq_len=64)
     layers = _layers(cfg, 2, 5)
-    stack = FP8EncoderStack(cfg, layers, cuda_device)
+    stack = FP8EncoderStack(cfg, layers, cuda_device, attention=attention)
     h = randn_f16((2, 64, cfg.d_model), 6)
     y = stack.forward(h.to(cuda_device)).float().cpu().view(-1)
     ref = ref_encoder.encoder_stack_ref(h, [ref_encoder.quantise_layer(lw) for lw in layers], cfg.heads)
@@ -121,9 +124,10 @@ def test_sliced_batch_matches_whole_batch(cuda_device):
         assert torch.equal(y[b0:b0 + 2], y_ref)
 
 
-def test_graphed_forward_matches_eager(cuda_device):
+@pytest.mark.parametrize("attention", ["wbk", "sdpa"])
+def test_graphed_forward_matches_eager(cuda_device, attention):
     cfg = EncoderConfig(layers=2, seq_len=96)
-    stack = FP8EncoderStack(cfg, _layers(cfg, 2, 13), cuda_device, slice_chunks=2)
+    stack = FP8EncoderStack(cfg, _layers(cfg, 2, 13), cuda_device, slice_chunks=2, attention=attention)
     h = randn_f16((3, 96, cfg.d_model), 14).to(cuda_device)
     y_eager = stack.forward(h).clone()
     y1 = stack.forward_graphed(h).clone()

@@ -35,8 +35,9 @@ UNITS = {
     "wbk_quant.cu": ["--use_fast_math"],
     "wbk_norm.cu": [],
     "wbk_gemm.cu": [],
+    "wbk_attn.cu": [],
 }
-HEADERS = [os.path.join(HERE, "wbk_common.cuh"), os.path.join(INCLUDE, "wbk.h")]
+HEADERS = [os.path.join(HERE, "wbk_common.cuh"), os.path.join(HERE, "wbk_sm100.cuh"), os.path.join(INCLUDE, "wbk.h")]
 
 
 def nvcc() -> str:

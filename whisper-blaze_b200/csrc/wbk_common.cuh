@@ -24,6 +24,9 @@ int sm_count();
 // Current device ordinal, or -1 on failure.
 int current_device();
 
+// Reads (and optionally clears) the device error word of the attention unit.
+int attn_read_device_error(uint32_t* v, bool clear);
+
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }

@@ -3,16 +3,18 @@
 Layer structure is HF WhisperEncoderLayer (pre-LN): LN -> self-attention ->
 +residual -> LN -> fc1 -> GELU(erf) -> fc2 -> +residual -> fp16 clamp, then a
 final LayerNorm after the last layer. q/k/v are one fused [3*D, D] projection
-(k has no bias, so its third of the bias is zero). Attention is torch SDPA in
-fp16 (the reference's own attention: HF runs it through torch SDPA).
+(k has no bias, so its third of the bias is zero). Attention runs in fp16 with
+fp32 softmax on the tcgen05 attention kernel (ops.attention) straight from the
+strided q/k/v views, which also reports max|out|; torch SDPA (what HF runs in
+the reference) is selectable for comparison.
 
 Per layer, on one stream and without any host synchronisation:
 
   LN1(h) -> fp8     -> xq  (fp8)  + scale              norm stats pass + norm quantise pass
                                                        (the fp16 LN output is never stored)
   QKV GEMM          -> qkv (fp16), bias epilogue       tcgen05 GEMM
-  SDPA(q, k, v)     -> a   (fp16)                      torch
-  amax+quantise(a)  -> aq  (fp8)                       2 kernels
+  attention(q,k,v)  -> a   (fp16) + max|a|             tcgen05 attention kernel
+  quantise(a)       -> aq  (fp8)
   out-proj GEMM     -> h2 = fp16(acc*s + b + h)        residual epilogue
   LN2(h2) -> fp8    -> x2q                             norm stats pass + norm quantise pass
   fc1 GEMM          -> y = fp16(acc*s + b) + max(y)          bias + max-key epilogue
@@ -23,6 +25,7 @@ Activation scales live in device memory; weights are quantised once.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 from typing import Callable, List, Optional
 
@@ -127,13 +130,22 @@ class FP8EncoderStack:
     """Encoder stack on one GPU. forward() takes [B, S, D] fp16 on the device."""
 
     def __init__(self, cfg: EncoderConfig, layers: List[LayerWeights], device,
-                 final_ln: Optional[tuple] = None, slice_chunks: Optional[int] = None) -> None:
+                 final_ln: Optional[tuple] = None, slice_chunks: Optional[int] = None,
+                 attention: Optional[str] = None) -> None:
         """slice_chunks: run the batch through the whole stack this many chunks at a
         time (None = all at once). Smaller slices keep each slice's [tokens, d_model]
         tensors (1500 x 1280 x 2 B = 3.84 MB per chunk) inside the 126 MB L2, so the
         passes that read a tensor twice (LayerNorm statistics then quantise,
-        amax then quantise) hit L2 on the second read."""
+        amax then quantise) hit L2 on the second read.
+
+        attention: "sdpa" (default; torch SDPA, cuDNN on B200, then an amax
+        pass) or "wbk" (the tcgen05 attention kernel, which also emits
+        max|out| for the following quantise); the WBK_ATTENTION environment
+        variable sets the default."""
         self.cfg = cfg
+        self.attention = attention or os.environ.get("WBK_ATTENTION", "sdpa")
+        if self.attention not in ("wbk", "sdpa"):
+            raise ValueError(f"attention must be 'wbk' or 'sdpa', not {self.attention!r}")
         self.slice_chunks = slice_chunks
         self.device = torch.device(device)
         self.layers: List[_QuantLayer] = []
@@ -188,17 +200,26 @@ class FP8EncoderStack:
         return out
 
     # -------------------------------------------------------------- compute
-    def _attention(self, qkv_buf: torch.Tensor, attn_buf: torch.Tensor, B: int, S: int) -> torch.Tensor:
+    def _attention(self, qkv_buf: torch.Tensor, attn_buf: torch.Tensor, B: int, S: int,
+                   amax_ws: torch.Tensor) -> torch.Tensor:
+        """Self-attention on the strided q/k/v views of the fused QKV output -> [T, D] fp16,
+        with max|out| max-accumulated into amax_ws."""
         cfg = self.cfg
         H, Dh = cfg.heads, cfg.head_dim
         qkv = qkv_buf.view(B, S, 3, H, Dh)
         q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
+        if self.attention == "wbk":
+            ops.attention(q, k, v, out=attn_buf.view(B, S, H, Dh).transpose(1, 2), out_amax=amax_ws)
+            return attn_buf
         o = F.scaled_dot_product_attention(q, k, v)  # [B, H, S, Dh]
         o = o.transpose(1, 2)
         if o.is_contiguous():
-            return o.reshape(B * S, cfg.d_model)
-        attn_buf.view(B, S, H, Dh).copy_(o)
-        return attn_buf
+            o = o.reshape(B * S, cfg.d_model)
+        else:
+            attn_buf.view(B, S, H, Dh).copy_(o)
+            o = attn_buf
+        ops.amax_accumulate(o, amax_ws)
+        return o
 
     def _layer(self, L: _QuantLayer, h: torch.Tensor, h_next: torch.Tensor, B: int, S: int,
                capture: Optional[dict] = None) -> None:
@@ -217,8 +238,7 @@ class FP8EncoderStack:
         keep("ln1_q", xq), keep("ln1_s", sc[0:1])
         self._gemm("qkv", 2 * T * D * 3 * D, xq, sc[0:1], L.w_qkv, L.s_qkv, L.b_qkv, out=qkv)
         keep("qkv", qkv)
-        attn = self._attention(qkv, attn_buf, B, S)
-        ops.amax_accumulate(attn, amax[1:2])
+        attn = self._attention(qkv, attn_buf, B, S, amax[1:2])
         ops.quantise_from_amax(attn, amax[1:2], q_out=aq, scale_out=sc[1:2])
         keep("attn", attn), keep("attn_q", aq), keep("attn_s", sc[1:2])
         self._gemm("out_proj", 2 * T * D * D, aq, sc[1:2], L.w_o, L.s_o, L.b_o, residual=h,

@@ -7,6 +7,7 @@ quantise -> GEMM -> norm -> quantise issues no host round trip.
 """
 from __future__ import annotations
 
+import ctypes
 from typing import Optional, Sequence, Union
 
 import torch
@@ -310,5 +311,44 @@ def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
         check(lib().wbk_gemm_fp8(a.data_ptr(), w.data_ptr(), M, N, K, fmt_code(a_format), fmt_code(w_format), alpha,
                                  pa, pw, ptr(bias), ptr(residual), o.data_ptr(), epi, ptr(out_amax), stream_of(a)),
               "gemm_fp8")
+    _count()
+    return o
+
+
+# ---------------------------------------------------------------- attention
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: Optional[torch.Tensor] = None,
+              scale: Optional[float] = None, out_amax: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Non-causal attention, head dim 64: softmax(q k^T * scale) v.
+
+    q [B, H, Sq, 64], k and v [B, H, Sk, 64] fp16 CUDA views (any strides that
+    are multiples of 8 elements, last dimension contiguous), e.g. the q/k/v
+    slices of a fused QKV projection; `out` likewise (default: a new contiguous
+    [B, H, Sq, 64] tensor). scale defaults to 1/sqrt(64). out_amax (optional, an
+    amax workspace) max-accumulates max|out|.
+    """
+    for t, name in ((q, "Q"), (k, "K"), (v, "V")):
+        require_cuda(t, name)
+        require_fp16(t, name)
+        if t.dim() != 4:
+            raise RuntimeError(f"{name} must be 4D: [B, H, S, D]")
+        if t.stride(-1) != 1:
+            raise RuntimeError(f"{name} must have a contiguous last dimension")
+    B, H, Sq, D = q.shape
+    if k.shape[:2] != (B, H) or v.shape[:2] != (B, H) or k.shape[-1] != D or v.shape[-1] != D:
+        raise RuntimeError("Q, K and V must agree in batch, heads and head dim")
+    if k.shape[2] != v.shape[2]:
+        raise RuntimeError("K and V must have the same sequence length")
+    Sk = k.shape[2]
+    o = torch.empty((B, H, Sq, D), dtype=torch.float16, device=q.device) if out is None else out
+    if o.shape != (B, H, Sq, D) or o.dtype != torch.float16 or o.stride(-1) != 1:
+        raise RuntimeError(f"out must be an fp16 [B, H, Sq, D] = {(B, H, Sq, D)} view with a contiguous last dimension")
+    require_same_device(q, k, v, o, out_amax)
+    strides = (ctypes.c_int64 * 12)(*(list(q.stride()[:3]) + list(k.stride()[:3]) + list(v.stride()[:3]) +
+                                      list(o.stride()[:3])))
+    sc = float(scale) if scale is not None else D ** -0.5
+    with torch.cuda.device(q.device):
+        check(lib().wbk_attention_f16(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), B, H, Sq, Sk, D,
+                                      strides, sc, ptr(out_amax), stream_of(q)), "attention")
     _count()
     return o

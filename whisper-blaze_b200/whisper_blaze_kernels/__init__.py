@@ -17,7 +17,10 @@ Differences that only remove hazards of the reference:
 
 Added (not in the reference): `gemm_fp8_e4m3` / `gemm_fp8`, the FP8 scaled GEMM
 the precision.py linear layers need, and `quantise_e4m3_dev`, which keeps the
-scale on the device instead of returning a Python float.
+scale on the device instead of returning a Python float. `encoder_self_attn`
+and `decoder_cross_attn` run a tcgen05 attention kernel (head dim 64) in place
+of the reference's unfinished ones; `decoder_self_attn` (causal) and
+`mel_spectrogram` raise NotImplementedError.
 """
 from __future__ import annotations
 
@@ -105,18 +108,40 @@ def gemm_fp8(a_fp8: torch.Tensor, a_scale, w_fp8: torch.Tensor, w_scale, bias: O
     return _ops.gemm_fp8(a_fp8, a_scale, w_fp8, w_scale, bias, residual, epilogue, a_format, w_format, out)
 
 
+def _attn_checks(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, q_only_fp16: bool) -> None:
+    # CHECK_INPUT (CUDA + contiguous) on all three, CHECK_FP16 as the reference binds
+    for t, name in ((Q, "Q"), (K, "K"), (V, "V")):
+        _ops.require_input(t, name)
+    _ops.require_fp16(Q, "Q")
+    if not q_only_fp16 or K.dtype != torch.float16 or V.dtype != torch.float16:
+        _ops.require_fp16(K, "K")
+        _ops.require_fp16(V, "V")
+
+
+def encoder_self_attn(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor) -> torch.Tensor:
+    """Encoder self-attention (no causal mask). [B,H,Sq,D] fp16, D = 64; scale 1/sqrt(D)."""
+    _attn_checks(Q, K, V, False)
+    if Q.dim() != 4:
+        raise RuntimeError("Q must be 4D: [B, H, Sq, D]")
+    return _ops.attention(Q, K, V)
+
+
+def decoder_cross_attn(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor) -> torch.Tensor:
+    """Decoder cross-attention (no mask). Q [B,H,Sq,D] from the decoder, K/V [B,H,Sk,D] from the encoder."""
+    _attn_checks(Q, K, V, True)
+    return _ops.attention(Q, K, V)
+
+
 def _out_of_scope(name: str):
     def fn(*args, **kwargs):
         raise NotImplementedError(
             f"whisper_blaze_kernels.{name} is outside the FP8 quantised-matmul path rebuilt for B200 "
-            f"(attention runs in torch SDPA, mel features in the HF processor)")
+            f"(causal decoder attention runs in torch SDPA, mel features in the HF processor)")
     fn.__name__ = name
     return fn
 
 
 mel_spectrogram = _out_of_scope("mel_spectrogram")
-encoder_self_attn = _out_of_scope("encoder_self_attn")
-decoder_cross_attn = _out_of_scope("decoder_cross_attn")
 decoder_self_attn = _out_of_scope("decoder_self_attn")
 
 __all__: List[str] = [
