@@ -9,11 +9,12 @@
 // replaces torch SDPA on the strided q/k/v views of the fused QKV output and
 // also reports max|out| for the quantiser that follows.
 //
-// Design (one persistent CTA per SM, 320 threads):
+// Design (one persistent CTA per SM, 384 threads):
 //   * a work unit = two 128-row query tiles of one (batch, head); units are
 //     dealt round-robin, consecutive CTAs take consecutive units of the same
 //     head so its K/V tiles are shared through L2;
-//   * warp 8: TMA producer. Q tiles and a 3-stage ring of K/V tiles
+//   * warp 8: TMA producer (warps 8-11 hand registers to the softmax
+//     warpgroups with setmaxnreg; 10 and 11 only take part in that). Q tiles and a 3-stage ring of K/V tiles
 //     [128 keys x 64 dims], 4-D tensor maps over (dim, position, head, batch)
 //     with 128-byte swizzle; rows past the sequence end read as zeros;
 //   * warp 9: TMEM owner + single-thread tcgen05.mma issuer (kind::f16).
@@ -23,11 +24,22 @@
 //     current tile's two PV products, so each softmax finds its next scores
 //     ready;
 //   * warps 0-3 / 4-7: one softmax warpgroup per query tile, one thread per
-//     query row (its TMEM lane). Scores -> row max -> exp2 -> fp16 P written
-//     to TMEM; the running max is only raised (and O rescaled in TMEM) when a
-//     tile's max exceeds it by more than 2^8, so rescaling is rare. At the end
-//     of a unit the warpgroup drains O, divides by the row sum, stores fp16
-//     rows and accumulates max|out|.
+//     query row (its TMEM lane), with most of the CTA's registers
+//     (setmaxnreg). Scores -> row max (3-input max) -> exp2 -> fp16 P written
+//     to TMEM, row sum in fp32 of the fp16 P values; the running max is only
+//     raised (and O rescaled in TMEM) when a tile's max exceeds it by more
+//     than 2^8, so rescaling is rare. Exponentials are ex2.approx.f32 by
+//     default, or ex2.approx.f16x2 (two per MUFU operation) with
+//     WBK_ATTN_EXP=f16. At the end of a unit the warpgroup drains O, divides
+//     by the row sum, stores fp16 rows and accumulates max|out|.
+//
+// Throughput (measured on B200): tcgen05.mma kind::f16 runs at the full
+// 8192 FLOP/clk per SM with both operands in shared memory and N >= 128, but
+// an MMA whose A operand is read from TMEM costs ~87 clocks per K=16 step
+// whatever N is, and N = 64 halves the rate. With head dim 64 the PV product
+// (N = 64, P from TMEM) therefore bounds this kernel at ~1900 clocks per
+// pair of 128 x 128 tiles, and in practice (softmax TMEM traffic alongside)
+// it runs at about half of that.
 // TMEM columns: S0 [0,128) S1 [128,256) P0 [256,320) P1 [320,384)
 // O0 [384,448) O1 [448,512).
 //
@@ -35,7 +47,9 @@
 // WBK_ERR_DEVICE_TIMEOUT in this unit's device word, raises the CTA abort
 // flag, and every role leaves its loop; in-flight copies and MMAs are drained
 // with bounded waits before TMEM is freed.
+#include <cstdlib>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "wbk_common.cuh"
@@ -49,7 +63,16 @@ constexpr int BQ = 128;                 // query rows per tile
 constexpr int BKV = 128;                // keys per tile
 constexpr int KV_STAGES = 3;
 constexpr int TILE_BYTES = BQ * HD * 2;  // 16 KB per Q, K or V tile
-constexpr int THREADS = 320;            // warps 0-7 softmax, 8 producer, 9 MMA
+constexpr int THREADS = 384;            // warps 0-7 softmax, 8 producer, 9 MMA, 10-11 idle
+// Register split (setmaxnreg): the launch gives every thread kLaunchRegs or
+// more (ptxas -v shows 168 for 384 threads); the producer/MMA warpgroup
+// gives registers back and the two softmax warpgroups take them:
+// 256 * kSoftmaxRegs + 128 * kControlRegs must not exceed 384 * the launch
+// count, which the host checks (kMinLaunchRegs) before every first launch.
+constexpr int kLaunchRegs = 168;
+constexpr int kSoftmaxRegs = 208;
+constexpr int kControlRegs = 80;
+constexpr int kMinLaunchRegs = (256 * kSoftmaxRegs + 128 * kControlRegs + THREADS - 1) / THREADS;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units
 
@@ -167,6 +190,42 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// Packed-fp16 pieces of the softmax: two fp32 -> one f16x2 (lo in the low
+// half), 2^x on both halves in one MUFU operation, and the fp32 row sum fed
+// straight from fp16 operands (sm_100 mixed-precision add), so the sum is of
+// exactly the fp16 P values the PV product uses.
+__device__ __forceinline__ uint32_t f16x2_pack(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+__device__ __forceinline__ uint32_t ex2_f16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+__device__ __forceinline__ float add_f16x2_f32(uint32_t h, float acc) {
+  float r;
+  asm("{\n\t.reg .f16 lo, hi;\n\t.reg .f32 t;\n\tmov.b32 {lo, hi}, %1;\n\t"
+      "add.f32.f16 t, lo, %2;\n\tadd.f32.f16 %0, hi, t;\n\t}"
+      : "=f"(r) : "r"(h), "f"(acc));
+  return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Bounded wait taken by a whole warp, with a warp-uniform result: every lane
+// leaves together, so the .sync.aligned tcgen05 loads and stores that follow
+// run on a converged warp, and a lane that saw the abort takes the others along.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                          uint64_t timeout_ns, uint32_t site) {
+  const bool ok = mbar_wait_inl(bar, parity, abort_flag, timeout_ns, site);
+  return __all_sync(0xFFFFFFFFu, ok);
+}
+
 __device__ __forceinline__ void unit_coords(const AttnParams& p, int u, int& b, int& h, int& q0) {
   const int bh = u / p.units_per_bh;
   q0 = (u - bh * p.units_per_bh) * 2 * BQ;
@@ -174,6 +233,9 @@ __device__ __forceinline__ void unit_coords(const AttnParams& p, int u, int& b, 
   h = bh - b * p.heads;
 }
 
+// kExpF16: exponentials as ex2.approx.f16x2 on fp16 arguments (two per MUFU
+// operation); otherwise ex2.approx.f32 on fp32 arguments, then rounded to fp16.
+template <bool kExpF16>
 __global__ void __launch_bounds__(THREADS, 1)
 attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_k,
                 const __grid_constant__ CUtensorMap tmap_v, const AttnParams p) {
@@ -216,7 +278,9 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
   const uint32_t tmem_base = s.tmem_base;
   const int n = p.kv_tiles;
 
-  if (warp == 8) {
+  if (warp >= 8) {
+   asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kControlRegs));
+   if (warp == 8) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       uint32_t g = 0;             // K/V tiles issued
@@ -226,7 +290,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         int b, h, q0;
         unit_coords(p, u, b, h, q0);
         for (int t = 0; t < 2 && ok; ++t) {
-          ok = mbar_wait(&s.q_empty[t], (q_loads[t] & 1u) ^ 1u, abort_flag, p.timeout_ns, ASITE_PRODUCER);
+          ok = mbar_wait_inl(&s.q_empty[t], (q_loads[t] & 1u) ^ 1u, abort_flag, p.timeout_ns, ASITE_PRODUCER);
           if (!ok) break;
           mbar_arrive_expect_tx(&s.q_full[t], TILE_BYTES);
           tma_load_4d(&tmap_q, &s.q_full[t], s.q[t], 0, q0 + t * BQ, h, b);
@@ -235,7 +299,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         for (int j = 0; j < n && ok; ++j) {
           const int st = static_cast<int>(g % KV_STAGES);
           const uint32_t ph = (g / KV_STAGES) & 1u;
-          ok = mbar_wait(&s.kv_empty[st], ph ^ 1u, abort_flag, p.timeout_ns, ASITE_PRODUCER);
+          ok = mbar_wait_inl(&s.kv_empty[st], ph ^ 1u, abort_flag, p.timeout_ns, ASITE_PRODUCER);
           if (!ok) break;
           mbar_arrive_expect_tx(&s.k_full[st], TILE_BYTES);
           tma_load_4d(&tmap_k, &s.k_full[st], s.k[st], 0, j * BKV, h, b);
@@ -248,10 +312,10 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         // Tail: every stage and Q buffer released, so no tcgen05.commit to this
         // CTA's barriers is still in flight when it exits.
         for (uint32_t i = 0, gt = g; i < KV_STAGES && ok; ++i, ++gt)
-          ok = mbar_wait(&s.kv_empty[gt % KV_STAGES], ((gt / KV_STAGES) & 1u) ^ 1u, abort_flag, p.timeout_ns,
+          ok = mbar_wait_inl(&s.kv_empty[gt % KV_STAGES], ((gt / KV_STAGES) & 1u) ^ 1u, abort_flag, p.timeout_ns,
                          ASITE_PRODUCER);
         for (int t = 0; t < 2 && ok; ++t)
-          ok = mbar_wait(&s.q_empty[t], (q_loads[t] & 1u) ^ 1u, abort_flag, p.timeout_ns, ASITE_PRODUCER);
+          ok = mbar_wait_inl(&s.q_empty[t], (q_loads[t] & 1u) ^ 1u, abort_flag, p.timeout_ns, ASITE_PRODUCER);
       }
       if (!ok) {
         // Abort path: let every copy already issued land before the CTA exits
@@ -260,15 +324,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         for (int i = 0; i < KV_STAGES; ++i) {
           const uint32_t fills = (g + KV_STAGES - 1 - static_cast<uint32_t>(i)) / KV_STAGES;  // loads into stage i
           if (fills > 0) {
-            mbar_wait(&s.k_full[i], (fills - 1) & 1u, &dummy, 1000000ull, ASITE_DRAIN);
-            mbar_wait(&s.v_full[i], (fills - 1) & 1u, &dummy, 1000000ull, ASITE_DRAIN);
+            mbar_wait_inl(&s.k_full[i], (fills - 1) & 1u, &dummy, 1000000ull, ASITE_DRAIN);
+            mbar_wait_inl(&s.v_full[i], (fills - 1) & 1u, &dummy, 1000000ull, ASITE_DRAIN);
           }
         }
         for (int t = 0; t < 2; ++t)
-          if (q_loads[t] > 0) mbar_wait(&s.q_full[t], (q_loads[t] - 1) & 1u, &dummy, 1000000ull, ASITE_DRAIN);
+          if (q_loads[t] > 0) mbar_wait_inl(&s.q_full[t], (q_loads[t] - 1) & 1u, &dummy, 1000000ull, ASITE_DRAIN);
       }
     }
-  } else if (warp == 9) {
+   } else if (warp == 9) {
     // ------------------------------------------------------- MMA issuer
     if (lane == 0) {
       uint32_t g = 0, ui = 0;
@@ -292,15 +356,15 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
       };
       for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x, ++ui) {
         for (int t = 0; t < 2 && ok; ++t)
-          ok = mbar_wait(&s.q_full[t], ui & 1u, abort_flag, p.timeout_ns, ASITE_MMA_Q);
+          ok = mbar_wait_inl(&s.q_full[t], ui & 1u, abort_flag, p.timeout_ns, ASITE_MMA_Q);
         if (!ok) break;
         // prologue: S_t of the unit's first KV tile
         {
           const int st = static_cast<int>(g % KV_STAGES);
-          ok = mbar_wait(&s.k_full[st], (g / KV_STAGES) & 1u, abort_flag, p.timeout_ns, ASITE_MMA_K);
+          ok = mbar_wait_inl(&s.k_full[st], (g / KV_STAGES) & 1u, abort_flag, p.timeout_ns, ASITE_MMA_K);
           if (!ok) break;
           for (int t = 0; t < 2 && ok; ++t) {
-            ok = mbar_wait(&s.s_free[t], (g & 1u) ^ 1u, abort_flag, p.timeout_ns, ASITE_MMA_SFREE);
+            ok = mbar_wait_inl(&s.s_free[t], (g & 1u) ^ 1u, abort_flag, p.timeout_ns, ASITE_MMA_SFREE);
             if (!ok) break;
             tc_fence_after();
             issue_s(t, st);
@@ -317,12 +381,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
           if (j + 1 < n) {
             const uint32_t gn = gj + 1;
             const int stn = static_cast<int>(gn % KV_STAGES);
-            if (!mbar_wait(&s.k_full[stn], (gn / KV_STAGES) & 1u, abort_flag, p.timeout_ns, ASITE_MMA_K)) {
+            if (!mbar_wait_inl(&s.k_full[stn], (gn / KV_STAGES) & 1u, abort_flag, p.timeout_ns, ASITE_MMA_K)) {
               ok = false;
               break;
             }
             for (int t = 0; t < 2 && ok; ++t) {
-              ok = mbar_wait(&s.s_free[t], gj & 1u, abort_flag, p.timeout_ns, ASITE_MMA_SFREE);
+              ok = mbar_wait_inl(&s.s_free[t], gj & 1u, abort_flag, p.timeout_ns, ASITE_MMA_SFREE);
               if (!ok) break;
               tc_fence_after();
               issue_s(t, stn);
@@ -333,13 +397,13 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
               umma_commit(&s.q_empty[1]);
             }
           }
-          if (!mbar_wait(&s.v_full[st], (gj / KV_STAGES) & 1u, abort_flag, p.timeout_ns, ASITE_MMA_V)) {
+          if (!mbar_wait_inl(&s.v_full[st], (gj / KV_STAGES) & 1u, abort_flag, p.timeout_ns, ASITE_MMA_V)) {
             ok = false;
             break;
           }
           for (int t = 0; t < 2 && ok; ++t) {
-            ok = mbar_wait(&s.p_full[t], gj & 1u, abort_flag, p.timeout_ns, ASITE_MMA_P);
-            if (ok && j == 0) ok = mbar_wait(&s.o_free[t], (ui & 1u) ^ 1u, abort_flag, p.timeout_ns, ASITE_MMA_OFREE);
+            ok = mbar_wait_inl(&s.p_full[t], gj & 1u, abort_flag, p.timeout_ns, ASITE_MMA_P);
+            if (ok && j == 0) ok = mbar_wait_inl(&s.o_free[t], (ui & 1u) ^ 1u, abort_flag, p.timeout_ns, ASITE_MMA_OFREE);
             if (!ok) break;
             tc_fence_after();
             issue_pv(t, st, j == 0);
@@ -353,10 +417,12 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         // Abort path: wait for every MMA this thread issued before TMEM is freed.
         umma_commit(&s.drain);
         int dummy = 0;
-        mbar_wait(&s.drain, 0, &dummy, 1000000ull, ASITE_DRAIN);
+        mbar_wait_inl(&s.drain, 0, &dummy, 1000000ull, ASITE_DRAIN);
       }
     }
+   }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kSoftmaxRegs));
     // --------------------------------------------------------- softmax
     const int t = warp >> 2;       // query tile of this warpgroup
     const int quarter = warp & 3;  // TMEM lanes 32*quarter ..
@@ -374,7 +440,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
       float l = 0.0f;       // running row sum of exp2(x - m)
       for (int j = 0; j < n; ++j) {
         const uint32_t gj = g + static_cast<uint32_t>(j);
-        if (!mbar_wait(&s.s_full[t], gj & 1u, abort_flag, p.timeout_ns, ASITE_SOFTMAX_S)) {
+        if (!warp_wait(&s.s_full[t], gj & 1u, abort_flag, p.timeout_ns, ASITE_SOFTMAX_S)) {
           ok = false;
           break;
         }
@@ -392,9 +458,16 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
           for (int c = 0; c < 128; ++c)
             if (c >= tail) x[c] = -INFINITY;
         }
-        float mx = x[0];
+        // Row max with 8 independent chains of 3-input max (a single chain of
+        // dependent maxima would leave the issue slots idle).
+        float mx8[8];
 #pragma unroll
-        for (int c = 1; c < 128; ++c) mx = fmaxf(mx, x[c]);
+        for (int i = 0; i < 8; ++i) mx8[i] = max3f(x[i], x[8 + i], x[16 + i]);
+#pragma unroll
+        for (int c = 24; c < 128; c += 16)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx8[i] = c + 8 + i < 128 ? max3f(mx8[i], x[c + i], x[c + 8 + i]) : fmaxf(mx8[i], x[c + i]);
+        const float mx = max3f(max3f(mx8[0], mx8[1], mx8[2]), max3f(mx8[3], mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]));
         const float mt = mx * sl2;
         float alpha = 1.0f;
         if (mt > m + kRescaleThreshold) {  // always true for the first tile (m = -inf)
@@ -404,19 +477,21 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
         l *= alpha;
         const bool rescale = (j > 0) && __any_sync(0xFFFFFFFFu, alpha != 1.0f);
         uint32_t pw[64];
-        float rs = 0.0f;
+        float rs8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const float p0 = ex2_approx(fmaf(x[2 * c], sl2, -m));
-          const float p1 = ex2_approx(fmaf(x[2 * c + 1], sl2, -m));
-          rs += p0 + p1;
-          const __half2 hp = __floats2half2_rn(p0, p1);
-          pw[c] = *reinterpret_cast<const uint32_t*>(&hp);
+          const float a0 = fmaf(x[2 * c], sl2, -m), a1 = fmaf(x[2 * c + 1], sl2, -m);
+          if (kExpF16) {
+            pw[c] = ex2_f16x2(f16x2_pack(a0, a1));
+          } else {
+            pw[c] = f16x2_pack(ex2_approx(a0), ex2_approx(a1));
+          }
+          rs8[c & 7] = add_f16x2_f32(pw[c], rs8[c & 7]);
         }
-        l += rs;
+        l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
         if (j > 0) {
           // P_t and O_t are free once the previous tile's PV product is done.
-          if (!mbar_wait(&s.pv_done[t], (gj - 1) & 1u, abort_flag, p.timeout_ns, ASITE_SOFTMAX_PV)) {
+          if (!warp_wait(&s.pv_done[t], (gj - 1) & 1u, abort_flag, p.timeout_ns, ASITE_SOFTMAX_PV)) {
             ok = false;
             break;
           }
@@ -443,7 +518,7 @@ attn_fwd_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constan
       if (!ok) break;
       // ---- unit epilogue: O_t / l -> fp16 rows
       const uint32_t glast = g + static_cast<uint32_t>(n) - 1u;
-      if (!mbar_wait(&s.pv_done[t], glast & 1u, abort_flag, p.timeout_ns, ASITE_SOFTMAX_PV)) break;
+      if (!warp_wait(&s.pv_done[t], glast & 1u, abort_flag, p.timeout_ns, ASITE_SOFTMAX_PV)) break;
       tc_fence_after();
       const int row = q0 + t * BQ + r;
       const float inv = 1.0f / l;
@@ -520,6 +595,34 @@ constexpr uint32_t idesc_f16(int M, int N, bool b_mn_major) {
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+template <bool kExpF16>
+int launch_attn(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const AttnParams& p, int grid,
+                cudaStream_t stream) {
+  static std::mutex mu;
+  static std::vector<char> configured;
+  const int dev = current_device();
+  if (dev < 0) return fail(WBK_ERR_CUDA, "no current CUDA device");
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
+    if (!configured[dev]) {
+      cudaFuncAttributes fa;
+      if (int e = cuda_check(cudaFuncGetAttributes(&fa, attn_fwd_kernel<kExpF16>), "attention function attributes"))
+        return e;
+      if (fa.numRegs < kMinLaunchRegs)  // the setmaxnreg split would wait for registers that do not exist
+        return fail(WBK_ERR_UNSUPPORTED, "attention kernel built with %d registers per thread, needs >= %d",
+                    fa.numRegs, kMinLaunchRegs);
+      if (int e = cuda_check(cudaFuncSetAttribute(attn_fwd_kernel<kExpF16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                  static_cast<int>(kSmemBytes)),
+                             "attention smem attribute"))
+        return e;
+      configured[dev] = 1;
+    }
+  }
+  attn_fwd_kernel<kExpF16><<<grid, THREADS, kSmemBytes, stream>>>(tq, tk, tv, p);
+  return cuda_check(cudaGetLastError(), "attention launch");
+}
+
 bool stride_ok(int64_t s) { return s > 0 && (s * 2) % 16 == 0 && (s * 2) < (int64_t(1) << 40); }
 
 }  // namespace
@@ -587,25 +690,14 @@ int wbk_attention_f16(const void* q, const void* k, const void* v, void* out, in
   p.idesc_o = idesc_f16(BQ, HD, true);
   p.timeout_ns = wait_timeout_ns();
 
-  static std::mutex mu;
-  static std::vector<char> configured;
-  const int dev = current_device();
-  if (dev < 0) return fail(WBK_ERR_CUDA, "no current CUDA device");
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
-    if (!configured[dev]) {
-      if (int e = cuda_check(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                  static_cast<int>(kSmemBytes)),
-                             "attention smem attribute"))
-        return e;
-      configured[dev] = 1;
-    }
-  }
+  static const bool exp_f16 = [] {
+    const char* e = std::getenv("WBK_ATTN_EXP");
+    return e != nullptr && std::string(e) == "f16";
+  }();
   const int sms = sm_count() > 0 ? sm_count() : 148;
   const int grid = p.num_units < sms ? p.num_units : sms;
-  attn_fwd_kernel<<<grid, THREADS, kSmemBytes, reinterpret_cast<cudaStream_t>(stream)>>>(tq, tk, tv, p);
-  return cuda_check(cudaGetLastError(), "attention launch");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return exp_f16 ? launch_attn<true>(tq, tk, tv, p, grid, st) : launch_attn<false>(tq, tk, tv, p, grid, st);
 }
 
 }  // extern "C"

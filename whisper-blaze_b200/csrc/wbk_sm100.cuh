@@ -64,8 +64,8 @@ __device__ __forceinline__ void record_device_error(uint32_t code, uint32_t site
 // Bounded wait: true when the phase with `parity` completed; false when the
 // CTA abort flag is raised or `timeout_ns` of wall clock passed (the latter
 // records the error and raises the abort flag). Iterations are capped too.
-__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
-                                            uint64_t timeout_ns, uint32_t site) {
+__device__ __forceinline__ bool mbar_wait_loop(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               uint64_t timeout_ns, uint32_t site) {
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 0; it < (1u << 30); ++it) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -79,10 +79,24 @@ __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, vola
   return false;
 }
 
+// Out-of-line copy, so the common (already complete) case stays small.
+__device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                            uint64_t timeout_ns, uint32_t site) {
+  return mbar_wait_loop(bar, parity, abort_flag, timeout_ns, site);
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           uint64_t timeout_ns, uint32_t site) {
   if (mbar_try_wait(bar, parity)) return true;
   return mbar_wait_slow(bar, parity, abort_flag, timeout_ns, site);
+}
+
+// Fully inlined bounded wait, for kernels that change their register count
+// with setmaxnreg (a called function cannot serve regions of different sizes).
+__device__ __forceinline__ bool mbar_wait_inl(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                              uint64_t timeout_ns, uint32_t site) {
+  if (mbar_try_wait(bar, parity)) return true;
+  return mbar_wait_loop(bar, parity, abort_flag, timeout_ns, site);
 }
 
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x, int y) {
