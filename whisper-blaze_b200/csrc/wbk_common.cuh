@@ -89,6 +89,17 @@ __device__ __forceinline__ uint32_t f16_from_order_key(uint32_t k) {
   return (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may start while the previous kernel in the
+// stream still runs; it calls griddep_wait() before touching anything that
+// kernel writes (the wait returns once the previous grid has completed and its
+// memory is visible). Producers call griddep_launch_dependents() to let such a
+// dependant start early. Both are no-ops for ordinary launches.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Streaming 16-byte global load (read once, keep L1 clean).
 __device__ __forceinline__ uint4 ld_stream16(const void* p) {
   uint4 r;

@@ -296,6 +296,9 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
   if (kPair) cluster_sync();  // the leader's barriers are initialised before the peer signals them
   tc_fence_after();
   const uint32_t tmem_base = s.tmem_base;
+  // Launched with programmatic stream serialization: everything above overlaps
+  // the kernel that produces A / the scales; nothing below runs before it is done.
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -560,6 +563,15 @@ int make_tmap(CUtensorMap* map, CUtensorMapDataType dtype, size_t elem_bytes, co
 }
 
 
+// Programmatic dependent launch of the GEMM (default on; WBK_PDL=0 turns it off).
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_PDL");
+    return e == nullptr || std::atoi(e) != 0;
+  }();
+  return on;
+}
+
 template <int kBN, int kEpi, bool kTma, bool kPair>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const Params& p, int grid,
                 cudaStream_t stream) {
@@ -580,12 +592,23 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
       configured[dev] = 1;
     }
   }
-  if (!kPair) {
-    kernel<<<grid, THREADS, kSmem, stream>>>(ta, tw, to, p);
-    return cuda_check(cudaGetLastError(), "fp8 gemm launch");
-  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int nattr = 0;
+  if (pdl_enabled()) {  // the kernel waits (griddep_wait) before reading anything a predecessor writes
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+  }
+  if (!kPair) {
+    cfg.attrs = attr;
+    cfg.numAttrs = nattr;
+    return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, p), "fp8 gemm launch");
+  }
   {
     // Persistent pairs: never launch more clusters than can be resident at once.
     static std::vector<int> max_clusters;
@@ -611,16 +634,13 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
     }
     if (grid > 2 * max_clusters[dev]) cfg.gridDim.x = static_cast<unsigned>(2 * max_clusters[dev]);
   }
-  cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = kSmem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
+  attr[nattr].id = cudaLaunchAttributeClusterDimension;
+  attr[nattr].val.clusterDim.x = 2;
+  attr[nattr].val.clusterDim.y = 1;
+  attr[nattr].val.clusterDim.z = 1;
+  ++nattr;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = nattr;
   return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, p), "fp8 gemm (CTA pair) launch");
 }
 

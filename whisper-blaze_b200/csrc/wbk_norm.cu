@@ -162,6 +162,7 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
                  const __half* __restrict__ beta, __half* __restrict__ out, __half* __restrict__ sum_out,
                  int64_t rows, int D, float eps, uint32_t* __restrict__ out_amax, float2* __restrict__ stats,
                  const float* __restrict__ scale_inv, uint8_t* __restrict__ q_out, float* __restrict__ scale_out) {
+  griddep_launch_dependents();  // a following GEMM may run its prologue meanwhile
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = D >> 3;
   const float fD = static_cast<float>(D);

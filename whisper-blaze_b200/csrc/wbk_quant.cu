@@ -109,6 +109,7 @@ template <int kFmt, bool kVec>
 __global__ void __launch_bounds__(kThreads)
 quantise_f16_kernel(const __half* __restrict__ x, int64_t n, const uint32_t* __restrict__ amax_bits,
                     float max_fp8, uint8_t* __restrict__ q, float* __restrict__ scale_out) {
+  griddep_launch_dependents();  // a following GEMM may run its prologue meanwhile
   float scale, inv;
   scale_from_amax(*amax_bits, max_fp8, scale, inv);
   if (scale_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
@@ -244,6 +245,7 @@ template <int kFmt, bool kVec>
 __global__ void __launch_bounds__(kGeluThreads, 1)
 quantise_gelu_kernel(const __half* __restrict__ y, int64_t n, const uint32_t* __restrict__ amax_bits,
                      float max_fp8, uint8_t* __restrict__ q, float* __restrict__ scale_out) {
+  griddep_launch_dependents();  // a following GEMM may run its prologue meanwhile
   extern __shared__ uint16_t gelu_table[];
   for (uint32_t h = threadIdx.x; h < 65536u; h += kGeluThreads) gelu_table[h] = static_cast<uint16_t>(gelu_f16_bits(h));
   float scale, inv;
@@ -317,6 +319,7 @@ template <int kFmt, bool kVec>
 __global__ void __launch_bounds__(kSmallThreads, 1)
 quantise_small_kernel(const __half* __restrict__ x, int64_t n, float max_fp8, uint8_t* __restrict__ q,
                       float* __restrict__ scale_out, uint32_t* __restrict__ amax_out) {
+  griddep_launch_dependents();  // a following GEMM may run its prologue meanwhile
   __shared__ uint32_t red[kSmallThreads / 32];
   __shared__ float sc[2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
