@@ -67,18 +67,55 @@ def fp8_peak(sustained: bool) -> tuple[float, str]:
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    """SM clock, power and clock-event (throttle) reasons of this rank's GPU, sampled every
+    10 ms through NVML on a background thread while the timed region runs (read-only queries);
+    falls back to `nvidia-smi -lms 200` when NVML is unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
+        self.thread = None
+        self.rows = []  # (sm_mhz, max_mhz, power_w, reason names)
         self.path = os.path.join("/tmp", f"wbk_clocks_{os.getpid()}.csv")
 
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.gpu).uuid)
+        return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+
+    def _poll(self, nv, h):
+        sm_id = nv.NVML_CLOCK_SM
+        max_mhz = nv.nvmlDeviceGetMaxClockInfo(h, sm_id)
+        masks = [(name, getattr(nv, attr)) for name, attr in self.REASONS]
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(h, sm_id)
+                watts = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                self.rows.append((float(mhz), float(max_mhz), watts, [n for n, m in masks if bits & m]))
+            except Exception:  # noqa: BLE001 - a failed query only loses a sample
+                pass
+            self._stop.wait(0.01)
+
     def __enter__(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            self._stop = threading.Event()
+            self.thread = threading.Thread(target=self._poll, args=(nv, h), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            self.thread = None
         try:
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
@@ -89,6 +126,9 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self._stop.set()
+            self.thread.join(5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -98,21 +138,26 @@ class ClockSampler:
             self.fh.close()
 
     def summary(self) -> dict:
-        if self.proc is None or not os.path.exists(self.path):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
-                    rows.append(parts)
+        if self.thread is not None:
+            rows = self.rows
+            src = "nvml 10 ms"
+        else:
+            rows = []
+            if self.proc is not None and os.path.exists(self.path):
+                names = [n for n, _ in self.REASONS]
+                with open(self.path) as f:
+                    for line in f:
+                        parts = [p.strip() for p in line.split(",")]
+                        if len(parts) >= 9 and parts[1].replace(".", "").isdigit():
+                            pw = float(parts[3]) if parts[3].replace(".", "").isdigit() else 0.0
+                            rows.append((float(parts[1]), float(parts[2]), pw,
+                                         [names[i] for i in range(4) if parts[5 + i].lower() == "active"]))
+            src = "nvidia-smi 200 ms"
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(r[1]) for r in rows]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(rows[0][2]), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())}
+        reasons = sorted({n for r in rows for n in r[3]})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": rows[0][1], "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(r[2] for r in rows), "sampler": src}
 
 
 def setup_dist():
