@@ -225,6 +225,26 @@ int wbk_attention_f16(const void* q, const void* k, const void* v, void* out,
                       int64_t batch, int64_t heads, int64_t seq_q, int64_t seq_k, int64_t head_dim,
                       const int64_t* strides, float scale, uint32_t* out_amax_bits, wbk_stream_t stream);
 
+/* wbk_gemm_fp8 with a split-K workspace. For very short-M shapes (M <= 32 rows,
+ * K >= 2048) whose 64-wide column tiles cannot cover the SMs, K is split into
+ * slices computed by different CTAs; each writes an fp32 partial into
+ * `workspace` and the last slice of each tile to finish sums the partials in
+ * slice order (bit-deterministic) and applies the epilogue. `workspace` (device,
+ * 256-byte aligned, at least wbk_gemm_fp8_ws_bytes(M, N, K) bytes) must be
+ * zero-filled before its first use; calls leave it reusable, but two calls must
+ * not use the same workspace concurrently. With workspace == NULL, or a shape
+ * that needs none, this is wbk_gemm_fp8. No reference counterpart (the
+ * reference binds no GEMM). */
+int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t K,
+                    int a_fmt, int w_fmt, float alpha,
+                    const float* a_scale, const float* w_scale,
+                    const void* bias, const void* residual, void* out,
+                    int epilogue, uint32_t* out_amax_bits,
+                    void* workspace, int64_t workspace_bytes, wbk_stream_t stream);
+
+/* Bytes of split-K workspace wbk_gemm_fp8_ws uses for this shape (0: none). */
+int64_t wbk_gemm_fp8_ws_bytes(int64_t M, int64_t N, int64_t K);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

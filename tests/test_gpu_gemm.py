@@ -150,3 +150,62 @@ def test_gemm_max_key_epilogue(cuda_device):
     assert key.item() == order_key_f16(float(y.float().max()))
     with pytest.raises(RuntimeError, match="requires out_amax"):
         ops.gemm_fp8(aq, sa, wq, sw, b, epilogue="bias_maxkey")
+
+
+# ---- split-K for short-M (decoder-step) shapes
+
+@pytest.mark.parametrize("M,N,K", [(32, 1280, 5120), (16, 1280, 5120), (8, 24, 2048), (1, 256, 8192),
+                                   (17, 640, 4096 + 16), (64, 1280, 1280)])
+@pytest.mark.parametrize("epi", ["none", "residual", "bias_maxkey"])
+def test_gemm_split_k(cuda_device, M, N, K, epi):
+    """K split over more CTAs than the 64-wide column tiles (every shape here but the last one
+    splits): same gate as the unsplit GEMM, bitwise deterministic across calls, and the
+    workspace is left reusable (tickets back at 0)."""
+    from whisper_blaze_b200 import _lib
+    need = _lib.lib().wbk_gemm_fp8_ws_bytes(M, N, K)
+    aq, sa, wq, sw, b = _operands(M, N, K, 7 * M + N + K, cuda_device)
+    res = randn_f16((M, N), 3).to(cuda_device) if epi == "residual" else None
+    key = ops.new_amax_ws(cuda_device) if epi == "bias_maxkey" else None
+    ws = torch.zeros(max(need, 1), dtype=torch.uint8, device=cuda_device)
+    y1 = ops.gemm_fp8(aq, sa, wq, sw, b, res, epi, out_amax=key, workspace=ws)
+    y2 = ops.gemm_fp8(aq, sa, wq, sw, b, res, epi, out_amax=key, workspace=ws)
+    assert torch.equal(y1, y2)
+    ref_epi = gemm.EPI_RESIDUAL if epi == "residual" else gemm.EPI_NONE
+    _check(y1, _ref(aq, sa, wq, sw, b, res, ref_epi))
+    y_unsplit = ops.gemm_fp8(aq, sa, wq, sw, b, res, epi, out_amax=key, split_k=False)
+    _check(y_unsplit, _ref(aq, sa, wq, sw, b, res, ref_epi))
+    if epi == "bias_maxkey":
+        from oracle.gemm import order_key_f16
+        assert key.item() == order_key_f16(float(y1.float().max()))
+    if need > 0:
+        # the ticket block (first 16 KB of the workspace) must be all zero again
+        assert int(ws[:16384].view(torch.int32).abs().sum().item()) == 0
+    assert _lib.device_error() == 0
+
+
+def test_gemm_split_k_workspace_errors(cuda_device):
+    from whisper_blaze_b200 import _lib
+    M, N, K = 16, 1280, 5120
+    need = _lib.lib().wbk_gemm_fp8_ws_bytes(M, N, K)
+    assert need > 0
+    assert _lib.lib().wbk_gemm_fp8_ws_bytes(4096, 1280, 1280) == 0  # large M: no split
+    assert _lib.lib().wbk_gemm_fp8_ws_bytes(16, 1280, 1280) == 0  # short K: no split
+    assert _lib.lib().wbk_gemm_fp8_ws_bytes(64, 1280, 5120) == 0  # M = 64: no split
+    aq, sa, wq, sw, b = _operands(M, N, K, 5, cuda_device)
+    small = torch.zeros(need // 2, dtype=torch.uint8, device=cuda_device)
+    with pytest.raises(RuntimeError, match="workspace"):
+        ops.gemm_fp8(aq, sa, wq, sw, b, workspace=small)
+
+
+def test_gemm_split_k_shared_workspace_across_shapes(cuda_device):
+    """One workspace serving several short-M shapes in turn (the decoder step does this):
+    the partials of one shape must never land on another shape's tickets."""
+    shapes = [(16, 3840, 2048), (32, 1280, 5120), (16, 2560, 5120), (64, 1280, 1280)]
+    ops_ = []
+    for i, (M, N, K) in enumerate(shapes):
+        aq, sa, wq, sw, b = _operands(M, N, K, 100 + i, cuda_device)
+        ops_.append((aq, sa, wq, sw, b, ops.gemm_fp8(aq, sa, wq, sw, b, split_k=False)))
+    for _ in range(3):
+        for aq, sa, wq, sw, b, ref in ops_:
+            y = ops.gemm_fp8(aq, sa, wq, sw, b)
+            assert gemm.rel_error(y.float().cpu(), ref.float().cpu()) <= 1e-2

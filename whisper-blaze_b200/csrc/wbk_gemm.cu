@@ -116,7 +116,18 @@ struct Params {
   uint32_t a_box_bytes;  // bytes one A box load delivers (64 or 128 rows x 128 B)
   uint32_t idesc;
   uint64_t timeout_ns;
+  // Split-K (64-wide tiles only): work item = (tile, K slice); num_items = num_tiles * splits.
+  int splits;
+  int num_items;
+  float* ws_partials;     // [num_items][128 rows][64 cols] fp32
+  uint32_t* ws_tickets;   // [num_tiles][EPI_WARPS] arrival counts, zero between calls
 };
+
+// K blocks [kb0, kb1) of split `split` (every split gets at least one when splits <= kblocks).
+__device__ __forceinline__ void split_range(const Params& p, int split, int& kb0, int& kb1) {
+  kb0 = static_cast<int>(static_cast<int64_t>(split) * p.kblocks / p.splits);
+  kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * p.kblocks / p.splits);
+}
 
 
 // ----------------------------------------------------------------- epilogue
@@ -306,10 +317,13 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_stride) {
+      for (int item = first_tile; item < p.num_items && ok; item += tile_stride) {
+        const int tile = item / p.splits;
+        int kb0, kb1;
+        split_range(p, item - tile * p.splits, kb0, kb1);
         const int m0 = (tile / p.tiles_n) * TL::ROWS + row_off;
         const int n0 = (tile % p.tiles_n) * kBN + static_cast<int>(rank) * TL::B_ROWS;
-        for (int kb = 0; kb < p.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) {
             ok = false;
             break;
@@ -360,14 +374,16 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_stride) {
+      for (int item = first_tile; item < p.num_items && ok; item += tile_stride) {
+        int kb0, kb1;
+        split_range(p, item % p.splits, kb0, kb1);
         if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1u, abort_flag, p.timeout_ns, SITE_MMA_ACC_EMPTY)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
-        for (int kb = 0; kb < p.kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&s.full[stage], phase, abort_flag, p.timeout_ns, SITE_MMA_FULL)) {
             ok = false;
             break;
@@ -380,9 +396,9 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
             // Advance the start address by k*32 bytes inside the 128-byte swizzle row.
             const uint64_t koff = static_cast<uint64_t>((k * UMMA_K) >> 4);
             if (kPair)
-              umma_f8f6f4_pair(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+              umma_f8f6f4_pair(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
             else
-              umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+              umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           // frees this smem stage (in both CTAs of a pair) once its MMAs retire
           if (kPair) umma_commit_pair_mc(&s.empty[stage], 0x3);
@@ -420,9 +436,11 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;  // staging buffer toggle (kTmaStore)
-    prefetch_residual_l2<kBN, kEpi>(p, first_tile, TL::ROWS, row_off, quarter, col_half, lane);
-    for (int tile = first_tile; tile < p.num_tiles; tile += tile_stride) {
-      prefetch_residual_l2<kBN, kEpi>(p, tile + tile_stride, TL::ROWS, row_off, quarter, col_half, lane);  // next tile
+    prefetch_residual_l2<kBN, kEpi>(p, first_tile / p.splits, TL::ROWS, row_off, quarter, col_half, lane);
+    for (int item = first_tile; item < p.num_items; item += tile_stride) {
+      const int tile = item / p.splits;
+      prefetch_residual_l2<kBN, kEpi>(p, (item + tile_stride) / p.splits, TL::ROWS, row_off, quarter, col_half,
+                                      lane);  // next tile
       const int m0 = (tile / p.tiles_n) * TL::ROWS + row_off;
       const int n0 = (tile % p.tiles_n) * kBN + col_half * TL::EPI_COLS;
       const int row0 = m0 + quarter * 32;
@@ -476,6 +494,80 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
           }
         }
       };
+      // Split-K: park this warp's fp32 partial (rows of its lane quarter, its
+      // columns) in the workspace; the warp whose ticket completes the tile's
+      // count sums every split's partial in split order (bit-deterministic) and
+      // runs the epilogue. Returns false when this warp has nothing to store.
+      auto split_reduce = [&](const uint32_t* regs, int c, uint32_t* sum) -> bool {
+        const int trow = quarter * 32 + lane;  // row inside the 128-row tile
+        const int tcol = col_half * TL::EPI_COLS + c * CHUNK;
+        const size_t stride_item = static_cast<size_t>(TL::ROWS) * kBN;
+        if (row < p.M) {
+          float4* dst = reinterpret_cast<float4*>(p.ws_partials + static_cast<size_t>(item) * stride_item +
+                                                  static_cast<size_t>(trow) * kBN + tcol);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(dst + q, make_float4(__uint_as_float(regs[4 * q]), __uint_as_float(regs[4 * q + 1]),
+                                        __uint_as_float(regs[4 * q + 2]), __uint_as_float(regs[4 * q + 3])));
+        }
+        __threadfence();
+        __syncwarp();
+        uint32_t last = 0;
+        if (lane == 0) {
+          constexpr int kChunks = TL::EPI_COLS / CHUNK;
+          uint32_t* t = p.ws_tickets + (static_cast<size_t>(tile) * EPI_WARPS + quarter * 2 + col_half) * kChunks + c;
+          last = atomicAdd(t, 1u) == static_cast<uint32_t>(p.splits - 1) ? 1u : 0u;
+          if (last) *t = 0u;  // every split has arrived: leave the ticket zero for the next call
+        }
+        last = __shfl_sync(0xFFFFFFFFu, last, 0);
+        if (!last) return false;
+        __threadfence();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sum[j] = 0u;
+        if (row < p.M) {
+          float f[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = 0.0f;
+          // Slices are added in order 0, 1, 2, ...; the loads of up to four slices are
+          // in flight together.
+          const float* base = p.ws_partials + static_cast<size_t>(tile) * p.splits * stride_item +
+                              static_cast<size_t>(trow) * kBN + tcol;
+          for (int sp = 0; sp < p.splits; sp += 4) {
+            float4 v4[4][8];
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (sp + u < p.splits) {
+                const float4* src = reinterpret_cast<const float4*>(base + static_cast<size_t>(sp + u) * stride_item);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) v4[u][q] = __ldcg(src + q);
+              }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+              if (sp + u < p.splits) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  f[4 * q] += v4[u][q].x;
+                  f[4 * q + 1] += v4[u][q].y;
+                  f[4 * q + 2] += v4[u][q].z;
+                  f[4 * q + 3] += v4[u][q].w;
+                }
+              }
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum[j] = __float_as_uint(f[j]);
+        }
+        return true;
+      };
+      auto finish = [&](const uint32_t* regs, const uint4* res, int c) {
+        if constexpr (kBN == 64 && !kPair) {  // split-K exists only for the 64-wide (short-M) tiles
+          if (p.splits > 1) {
+            uint32_t sum[32];
+            if (split_reduce(regs, c, sum)) process(sum, res, c);
+            return;
+          }
+        }
+        process(regs, res, c);
+      };
       // Double-buffered drain: the TMEM load and the residual loads of chunk c+1
       // are in flight while chunk c is processed.
       uint32_t ra[32], rb[32];
@@ -490,14 +582,14 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
           tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>((c + 1) * CHUNK), rb);
           prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 1) * CHUNK, resb);
         }
-        process(ra, resa, c);
+        finish(ra, resa, c);
         if (more1) {
           tmem_ld_wait(rb);
           if (more2) {
             tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>((c + 2) * CHUNK), ra);
             prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 2) * CHUNK, resa);
           }
-          process(rb, resb, c + 1);
+          finish(rb, resb, c + 1);
           if (more2) tmem_ld_wait(ra);
         }
       }
@@ -681,6 +773,37 @@ int pick_bn(int64_t M, int64_t N, int sms) {
   return 128;
 }
 
+// The ticket block has one fixed size for every shape (split-K needs 2 * tiles <= SMs,
+// so at most 512 tiles), so the partials of one shape never overlap the tickets of
+// another sharing the workspace.
+constexpr int kMaxSplitTiles = 512;
+// Split-K plan for short-M GEMMs (64-wide tiles): K slices per tile so the
+// (tile, slice) work items cover the SMs. Measured on B200, splitting pays only
+// when each CTA would otherwise stream a long K for very few rows (M <= 32,
+// K >= 2048, at least 4 K blocks per slice: M = 16 or 1, N = 1280, K = 5120 ran
+// ~7 % faster); at M = 64 the fp32 partial round trip costs more than the
+// shorter K loop saves (N = 1280, K = 5120: 24.6 us split vs 17.7 us), so the
+// plan is 1 there.
+void splitk_plan(int64_t M, int64_t N, int64_t K, int* splits, int* tiles) {
+  *splits = 1;
+  *tiles = 0;
+  if (M <= 0 || N <= 0 || K <= 0 || M > 32) return;
+  const int sms = sm_count() > 0 ? sm_count() : 148;
+  const int64_t t = (N + 63) / 64;
+  const int64_t kblocks = (K + BK - 1) / BK;
+  *tiles = static_cast<int>(t);
+  if (2 * t > sms || t > kMaxSplitTiles || kblocks < 16) return;
+  int64_t sp = sms / t;
+  if (sp > kblocks / 4) sp = kblocks / 4;
+  if (sp > 16) sp = 16;
+  *splits = static_cast<int>(sp < 1 ? 1 : sp);
+}
+int64_t splitk_ticket_bytes(int /*tiles*/) { return static_cast<int64_t>(kMaxSplitTiles) * EPI_WARPS * 4; }
+int64_t splitk_ws_bytes(int splits, int tiles) {
+  if (splits <= 1) return 0;
+  return splitk_ticket_bytes(tiles) + static_cast<int64_t>(tiles) * splits * BM * 64 * 4;
+}
+
 }  // namespace
 }  // namespace wbk
 
@@ -688,9 +811,23 @@ using namespace wbk;
 
 extern "C" {
 
+int64_t wbk_gemm_fp8_ws_bytes(int64_t M, int64_t N, int64_t K) {
+  int splits = 0, tiles = 0;
+  splitk_plan(M, N, K, &splits, &tiles);
+  return splitk_ws_bytes(splits, tiles);
+}
+
 int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int a_fmt, int w_fmt, float alpha,
                  const float* a_scale, const float* w_scale, const void* bias, const void* residual, void* out,
                  int epilogue, uint32_t* out_amax_bits, wbk_stream_t stream) {
+  return wbk_gemm_fp8_ws(A, W, M, N, K, a_fmt, w_fmt, alpha, a_scale, w_scale, bias, residual, out, epilogue,
+                         out_amax_bits, nullptr, 0, stream);
+}
+
+int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int a_fmt, int w_fmt, float alpha,
+                    const float* a_scale, const float* w_scale, const void* bias, const void* residual, void* out,
+                    int epilogue, uint32_t* out_amax_bits, void* workspace, int64_t workspace_bytes,
+                    wbk_stream_t stream) {
   if (M < 0 || N <= 0 || K <= 0)
     return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
                 (long long)K);
@@ -745,6 +882,25 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, 
   if (num_tiles > INT32_MAX) return fail(WBK_ERR_UNSUPPORTED, "wbk_gemm_fp8: too many tiles");
   p.num_tiles = static_cast<int>(num_tiles);
   p.kblocks = static_cast<int>((K + BK - 1) / BK);
+  // Split-K for the narrow-tile (short-M) shapes when the caller gave a workspace.
+  p.splits = 1;
+  p.ws_partials = nullptr;
+  p.ws_tickets = nullptr;
+  if (workspace != nullptr && !pair && bn == 64) {
+    int splits = 1, tiles = 0;
+    splitk_plan(M, N, K, &splits, &tiles);
+    const int64_t need = splitk_ws_bytes(splits, tiles);
+    if (splits > 1) {
+      if (!aligned(workspace, 256)) return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8_ws: workspace must be 256-byte aligned");
+      if (workspace_bytes < need)
+        return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8_ws: workspace of %lld bytes, needs %lld",
+                    (long long)workspace_bytes, (long long)need);
+      p.splits = splits;
+      p.ws_tickets = static_cast<uint32_t*>(workspace);
+      p.ws_partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + splitk_ticket_bytes(tiles));
+    }
+  }
+  p.num_items = p.num_tiles * p.splits;
   p.alpha = alpha;
   p.a_scale = a_scale;
   p.w_scale = w_scale;
@@ -766,7 +922,7 @@ int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, 
     const int grid = 2 * static_cast<int>(num_tiles < pairs ? num_tiles : pairs);
     return dispatch_epi<256, true>(epilogue, vec, ta, tw, to, p, grid, s);
   }
-  const int grid = static_cast<int>(num_tiles < sms ? num_tiles : sms);
+  const int grid = p.num_items < sms ? p.num_items : sms;
   if (bn == 64) return dispatch_epi<64>(epilogue, vec, ta, tw, to, p, grid, s);
   if (bn == 128) return dispatch_epi<128>(epilogue, vec, ta, tw, to, p, grid, s);
   return dispatch_epi<256>(epilogue, vec, ta, tw, to, p, grid, s);

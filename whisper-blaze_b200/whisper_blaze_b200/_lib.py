@@ -52,6 +52,9 @@ _PROTOTYPES = {
     "wbk_rmsnorm_f16": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _f32, _vp]),
     "wbk_gemm_fp8": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _i32, _f32, _vp, _vp, _vp, _vp, _vp, _i32, _vp, _vp]),
     "wbk_attention_f16": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _f32, _vp, _vp]),
+    "wbk_gemm_fp8_ws": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _i32, _f32, _vp, _vp, _vp, _vp, _vp, _i32, _vp,
+                               _vp, _i64, _vp]),
+    "wbk_gemm_fp8_ws_bytes": (_i64, [_i64, _i64, _i64]),
 }
 
 _lock = threading.Lock()

@@ -263,16 +263,39 @@ def _scale_arg(scale: Scale, name: str, device) -> tuple[float, Optional[int]]:
     return float(scale), None
 
 
+_SPLITK_WS: dict = {}
+
+
+def splitk_workspace(device, nbytes: int) -> Optional[torch.Tensor]:
+    """The per-device split-K workspace (zero-filled once, grown on demand).
+
+    Shared by every short-M GEMM on the device, so such GEMMs must not run
+    concurrently on different streams; pass `workspace=` to gemm_fp8 to give a
+    stream its own."""
+    if nbytes <= 0:
+        return None
+    dev = torch.device(device)
+    ws = _SPLITK_WS.get(dev)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        _SPLITK_WS[dev] = ws
+    return ws
+
+
 def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
              bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None, epilogue="none",
              a_format="e4m3", w_format="e4m3", out: Optional[torch.Tensor] = None,
-             out_amax: Optional[torch.Tensor] = None) -> torch.Tensor:
+             out_amax: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+             split_k: bool = True) -> torch.Tensor:
     """out[..., N] = epilogue(dq(a)[..., K] @ dq(w)[N, K]^T + bias); fp16 output.
 
     a: fp8 codes [..., K]; w: fp8 codes [N, K] (nn.Linear layout); scales as
     Python floats or 1-element fp32 CUDA tensors; epilogue one of
     'none' | 'gelu' | 'residual' | 'residual_clamp' | 'bias_maxkey' (bias only, and
     out_amax receives the order key of the largest output, for quantise_gelu).
+    Short-M shapes (M <= 128) split K over more SMs (split_k=True) using
+    `workspace` (a zero-filled uint8 CUDA tensor of at least
+    wbk_gemm_fp8_ws_bytes bytes) or the device's shared one.
     """
     require_input(a, "a_fp8")
     require_input(w, "w_fp8")
@@ -306,10 +329,15 @@ def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
     alpha_w, pw = _scale_arg(w_scale, "w_scale", a.device)
     alpha = float(torch.tensor(alpha_a, dtype=torch.float32) * torch.tensor(alpha_w, dtype=torch.float32))
     o = torch.empty(out_shape, dtype=torch.float16, device=a.device) if out is None else out
-    require_same_device(a, w, bias, residual, o, out_amax)
+    require_same_device(a, w, bias, residual, o, out_amax, workspace)
     with torch.cuda.device(a.device):
-        check(lib().wbk_gemm_fp8(a.data_ptr(), w.data_ptr(), M, N, K, fmt_code(a_format), fmt_code(w_format), alpha,
-                                 pa, pw, ptr(bias), ptr(residual), o.data_ptr(), epi, ptr(out_amax), stream_of(a)),
+        ws = None
+        if split_k and 0 < M <= 128:
+            need = lib().wbk_gemm_fp8_ws_bytes(M, N, K)
+            ws = workspace if workspace is not None else splitk_workspace(a.device, need)
+        check(lib().wbk_gemm_fp8_ws(a.data_ptr(), w.data_ptr(), M, N, K, fmt_code(a_format), fmt_code(w_format),
+                                    alpha, pa, pw, ptr(bias), ptr(residual), o.data_ptr(), epi, ptr(out_amax),
+                                    ptr(ws), 0 if ws is None else ws.numel(), stream_of(a)),
               "gemm_fp8")
     _count()
     return o
