@@ -48,7 +48,6 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 128;  // bytes of K per stage = fp8 elements = one 128-byte swizzle row
 constexpr int UMMA_K = 32;
-constexpr int A_STAGE_BYTES = BM * BK;  // 16 KB
 constexpr int NUM_ACC = 2;
 constexpr int EPI_WARPS = 8;
 constexpr int THREADS = 64 + EPI_WARPS * 32;  // 320
@@ -63,8 +62,15 @@ constexpr int STAGE_OUT_BYTES = 32 * CHUNK * 2;  // 32 rows x 32 fp16 = 2 KB
 // lower than one CTA computing 128 x kBN.
 template <int kBN, bool kPair = false>
 struct Tile {
-  static constexpr int B_ROWS = kPair ? kBN / 2 : kBN;  // weight rows this CTA loads per stage
-  static constexpr int B_STAGE_BYTES = B_ROWS * BK;     // 32 / 16 / 8 KB (16 KB per CTA in a pair)
+  static constexpr int B_ROWS = kPair ? kBN / 2 : kBN;  // weight rows this CTA loads per K block
+  static constexpr int B_SUB_BYTES = B_ROWS * BK;       // 32 / 16 / 8 KB (16 KB per CTA in a pair)
+  // K blocks per pipeline stage: one TMA load per operand and one full/empty
+  // barrier round trip serve G K blocks, so the single producer and MMA
+  // threads spend 1/G of the per-block issue cost (each barrier operation or
+  // TMA issue costs ~30-60 ns of one thread's time).
+  static constexpr int G = kBN == 64 ? 4 : 2;
+  static constexpr int A_STAGE_BYTES = G * BM * BK;     // room for G 128-row A blocks
+  static constexpr int B_STAGE_BYTES = G * B_SUB_BYTES;
   // Shared-memory ring depth: ~192 KB of operands in flight per SM whatever the shape.
   static constexpr int STAGES = (192 * 1024) / (A_STAGE_BYTES + B_STAGE_BYTES);
   static constexpr int TMEM_COLS = NUM_ACC * kBN;    // 512 / 256 / 128 (power of two >= 32)
@@ -85,7 +91,7 @@ enum : uint32_t {
 
 template <int kBN, bool kPair = false>
 struct SharedStorage {
-  uint8_t a[Tile<kBN, kPair>::STAGES][A_STAGE_BYTES];  // 1024-byte aligned (swizzle atom)
+  uint8_t a[Tile<kBN, kPair>::STAGES][Tile<kBN, kPair>::A_STAGE_BYTES];  // 1024-byte aligned (swizzle atom)
   uint8_t b[Tile<kBN, kPair>::STAGES][Tile<kBN, kPair>::B_STAGE_BYTES];
   uint8_t out[EPI_WARPS][2][STAGE_OUT_BYTES];  // per-warp double-buffered store staging
   uint64_t full[Tile<kBN, kPair>::STAGES];
@@ -113,7 +119,8 @@ struct Params {
   __half* out;
   uint32_t* out_amax;
   int out_pairs;  // direct-store path: rows 4-byte aligned, store fp16 pairs
-  uint32_t a_box_bytes;  // bytes one A box load delivers (64 or 128 rows x 128 B)
+  uint32_t a_box_bytes;  // bytes of one A K block (64 or 128 rows x 128 B); A blocks are this far apart in a stage
+  int grouped;           // 1: one 3-D TMA load per operand per stage (K % 128 == 0); 0: G 2-D loads
   uint32_t idesc;
   uint64_t timeout_ns;
   // Split-K (64-wide tiles only): work item = (tile, K slice); num_items = num_tiles * splits.
@@ -123,10 +130,13 @@ struct Params {
   uint32_t* ws_tickets;   // [num_tiles][EPI_WARPS] arrival counts, zero between calls
 };
 
-// K blocks [kb0, kb1) of split `split` (every split gets at least one when splits <= kblocks).
-__device__ __forceinline__ void split_range(const Params& p, int split, int& kb0, int& kb1) {
-  kb0 = static_cast<int>(static_cast<int64_t>(split) * p.kblocks / p.splits);
-  kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * p.kblocks / p.splits);
+// K blocks [kb0, kb1) of split `split`, whole stages of g blocks (every split
+// gets at least one stage when splits <= stages).
+__device__ __forceinline__ void split_range(const Params& p, int g, int split, int& kb0, int& kb1) {
+  const int64_t nst = (p.kblocks + g - 1) / g;
+  kb0 = static_cast<int>(static_cast<int64_t>(split) * nst / p.splits) * g;
+  kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * nst / p.splits) * g;
+  if (kb1 > p.kblocks) kb1 = p.kblocks;
 }
 
 
@@ -263,7 +273,8 @@ __device__ __forceinline__ float absmax_valid(float m, const float* v, int valid
 template <int kBN, int kEpi, bool kTmaStore, bool kPair>
 __global__ void __launch_bounds__(THREADS, 1)
 fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
-                const __grid_constant__ CUtensorMap tmap_out, const Params p) {
+                const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_a3,
+                const __grid_constant__ CUtensorMap tmap_w3, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   SharedStorage<kBN, kPair>& s =
       *reinterpret_cast<SharedStorage<kBN, kPair>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -289,8 +300,13 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     mbar_init(&s.drain, 1);
     s.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    prefetch_tmap(&tmap_a);
-    prefetch_tmap(&tmap_w);
+    if (p.grouped) {
+      prefetch_tmap(&tmap_a3);
+      prefetch_tmap(&tmap_w3);
+    } else {
+      prefetch_tmap(&tmap_a);
+      prefetch_tmap(&tmap_w);
+    }
     if (kTmaStore) prefetch_tmap(&tmap_out);
   }
   if (warp == 1) {
@@ -320,24 +336,42 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       for (int item = first_tile; item < p.num_items && ok; item += tile_stride) {
         const int tile = item / p.splits;
         int kb0, kb1;
-        split_range(p, item - tile * p.splits, kb0, kb1);
+        split_range(p, TL::G, item - tile * p.splits, kb0, kb1);
         const int m0 = (tile / p.tiles_n) * TL::ROWS + row_off;
         const int n0 = (tile % p.tiles_n) * kBN + static_cast<int>(rank) * TL::B_ROWS;
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kb = kb0; kb < kb1; kb += TL::G) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) {
             ok = false;
             break;
           }
+          // A stage always receives G whole boxes per operand (blocks past K read as zeros).
+          const uint32_t stage_bytes = TL::G * (p.a_box_bytes + TL::B_SUB_BYTES);
           if (kPair) {
             // Both CTAs' loads complete on the leader's full barrier, which expects both halves.
-            if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * (p.a_box_bytes + TL::B_STAGE_BYTES));
+            if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * stage_bytes);
             const uint32_t full_leader = mapa_shared(&s.full[stage], 0);
-            tma_load_2d_pair(&tmap_a, full_leader, s.a[stage], kb * BK, m0);
-            tma_load_2d_pair(&tmap_w, full_leader, s.b[stage], kb * BK, n0);
+            if (p.grouped) {
+              tma_load_3d_pair(&tmap_a3, full_leader, s.a[stage], 0, m0, kb);
+              tma_load_3d_pair(&tmap_w3, full_leader, s.b[stage], 0, n0, kb);
+            } else {
+#pragma unroll
+              for (int g = 0; g < TL::G; ++g) {
+                tma_load_2d_pair(&tmap_a, full_leader, s.a[stage] + g * p.a_box_bytes, (kb + g) * BK, m0);
+                tma_load_2d_pair(&tmap_w, full_leader, s.b[stage] + g * TL::B_SUB_BYTES, (kb + g) * BK, n0);
+              }
+            }
           } else {
-            mbar_arrive_expect_tx(&s.full[stage], p.a_box_bytes + TL::B_STAGE_BYTES);
-            tma_load_2d(&tmap_a, &s.full[stage], s.a[stage], kb * BK, m0);
-            tma_load_2d(&tmap_w, &s.full[stage], s.b[stage], kb * BK, n0);
+            mbar_arrive_expect_tx(&s.full[stage], stage_bytes);
+            if (p.grouped) {
+              tma_load_3d(&tmap_a3, &s.full[stage], s.a[stage], 0, m0, kb);
+              tma_load_3d(&tmap_w3, &s.full[stage], s.b[stage], 0, n0, kb);
+            } else {
+#pragma unroll
+              for (int g = 0; g < TL::G; ++g) {
+                tma_load_2d(&tmap_a, &s.full[stage], s.a[stage] + g * p.a_box_bytes, (kb + g) * BK, m0);
+                tma_load_2d(&tmap_w, &s.full[stage], s.b[stage] + g * TL::B_SUB_BYTES, (kb + g) * BK, n0);
+              }
+            }
           }
           if (++stage == TL::STAGES) {
             stage = 0;
@@ -376,29 +410,34 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       bool ok = true;
       for (int item = first_tile; item < p.num_items && ok; item += tile_stride) {
         int kb0, kb1;
-        split_range(p, item % p.splits, kb0, kb1);
+        split_range(p, TL::G, item % p.splits, kb0, kb1);
         if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1u, abort_flag, p.timeout_ns, SITE_MMA_ACC_EMPTY)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        for (int kbs = kb0; kbs < kb1; kbs += TL::G) {
           if (!mbar_wait(&s.full[stage], phase, abort_flag, p.timeout_ns, SITE_MMA_FULL)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = make_sw128_desc(s.a[stage]);
-          const uint64_t bdesc = make_sw128_desc(s.b[stage]);
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k) {
-            // Advance the start address by k*32 bytes inside the 128-byte swizzle row.
-            const uint64_t koff = static_cast<uint64_t>((k * UMMA_K) >> 4);
-            if (kPair)
-              umma_f8f6f4_pair(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
-            else
-              umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+          for (int g = 0; g < TL::G; ++g) {
+            const int kb = kbs + g;
+            if (kb >= kb1) break;
+            const uint64_t adesc = make_sw128_desc(s.a[stage] + g * p.a_box_bytes);
+            const uint64_t bdesc = make_sw128_desc(s.b[stage] + g * TL::B_SUB_BYTES);
+#pragma unroll
+            for (int k = 0; k < BK / UMMA_K; ++k) {
+              // Advance the start address by k*32 bytes inside the 128-byte swizzle row.
+              const uint64_t koff = static_cast<uint64_t>((k * UMMA_K) >> 4);
+              if (kPair)
+                umma_f8f6f4_pair(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+              else
+                umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+            }
           }
           // frees this smem stage (in both CTAs of a pair) once its MMAs retire
           if (kPair) umma_commit_pair_mc(&s.empty[stage], 0x3);
@@ -528,21 +567,21 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
           float f[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) f[j] = 0.0f;
-          // Slices are added in order 0, 1, 2, ...; the loads of up to four slices are
-          // in flight together.
+          // Slices are added in order 0, 1, 2, ...; the loads of two slices are in
+          // flight together (more would spill the epilogue's registers).
           const float* base = p.ws_partials + static_cast<size_t>(tile) * p.splits * stride_item +
                               static_cast<size_t>(trow) * kBN + tcol;
-          for (int sp = 0; sp < p.splits; sp += 4) {
-            float4 v4[4][8];
+          for (int sp = 0; sp < p.splits; sp += 2) {
+            float4 v4[2][8];
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < 2; ++u)
               if (sp + u < p.splits) {
                 const float4* src = reinterpret_cast<const float4*>(base + static_cast<size_t>(sp + u) * stride_item);
 #pragma unroll
                 for (int q = 0; q < 8; ++q) v4[u][q] = __ldcg(src + q);
               }
 #pragma unroll
-            for (int u = 0; u < 4; ++u)
+            for (int u = 0; u < 2; ++u)
               if (sp + u < p.splits) {
 #pragma unroll
                 for (int q = 0; q < 8; ++q) {
@@ -665,8 +704,8 @@ bool pdl_enabled() {
 }
 
 template <int kBN, int kEpi, bool kTma, bool kPair>
-int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const Params& p, int grid,
-                cudaStream_t stream) {
+int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const CUtensorMap& ta3,
+                const CUtensorMap& tw3, const Params& p, int grid, cudaStream_t stream) {
   static std::mutex mu;
   static std::vector<char> configured;
   const int dev = current_device();
@@ -699,7 +738,7 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
   if (!kPair) {
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
-    return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, p), "fp8 gemm launch");
+    return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, ta3, tw3, p), "fp8 gemm launch");
   }
   {
     // Persistent pairs: never launch more clusters than can be resident at once.
@@ -733,27 +772,56 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
   ++nattr;
   cfg.attrs = attr;
   cfg.numAttrs = nattr;
-  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, p), "fp8 gemm (CTA pair) launch");
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, ta3, tw3, p), "fp8 gemm (CTA pair) launch");
 }
 
+struct Maps {
+  CUtensorMap a, w, out, a3, w3;
+};
+
 template <int kBN, int kEpi, bool kPair>
-int dispatch_store(bool tma, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const Params& p,
-                   int grid, cudaStream_t s) {
-  return tma ? launch_gemm<kBN, kEpi, true, kPair>(ta, tw, to, p, grid, s)
-             : launch_gemm<kBN, kEpi, false, kPair>(ta, tw, to, p, grid, s);
+int dispatch_store(bool tma, const Maps& m, const Params& p, int grid, cudaStream_t s) {
+  return tma ? launch_gemm<kBN, kEpi, true, kPair>(m.a, m.w, m.out, m.a3, m.w3, p, grid, s)
+             : launch_gemm<kBN, kEpi, false, kPair>(m.a, m.w, m.out, m.a3, m.w3, p, grid, s);
 }
 
 template <int kBN, bool kPair = false>
-int dispatch_epi(int epilogue, bool tma, const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to,
-                 const Params& p, int grid, cudaStream_t s) {
+int dispatch_epi(int epilogue, bool tma, const Maps& m, const Params& p, int grid, cudaStream_t s) {
   switch (epilogue) {
-    case WBK_EPI_NONE: return dispatch_store<kBN, WBK_EPI_NONE, kPair>(tma, ta, tw, to, p, grid, s);
-    case WBK_EPI_GELU: return dispatch_store<kBN, WBK_EPI_GELU, kPair>(tma, ta, tw, to, p, grid, s);
-    case WBK_EPI_RESIDUAL: return dispatch_store<kBN, WBK_EPI_RESIDUAL, kPair>(tma, ta, tw, to, p, grid, s);
-    case WBK_EPI_RESIDUAL_CLAMP:
-      return dispatch_store<kBN, WBK_EPI_RESIDUAL_CLAMP, kPair>(tma, ta, tw, to, p, grid, s);
-    default: return dispatch_store<kBN, WBK_EPI_BIAS_MAXKEY, kPair>(tma, ta, tw, to, p, grid, s);
+    case WBK_EPI_NONE: return dispatch_store<kBN, WBK_EPI_NONE, kPair>(tma, m, p, grid, s);
+    case WBK_EPI_GELU: return dispatch_store<kBN, WBK_EPI_GELU, kPair>(tma, m, p, grid, s);
+    case WBK_EPI_RESIDUAL: return dispatch_store<kBN, WBK_EPI_RESIDUAL, kPair>(tma, m, p, grid, s);
+    case WBK_EPI_RESIDUAL_CLAMP: return dispatch_store<kBN, WBK_EPI_RESIDUAL_CLAMP, kPair>(tma, m, p, grid, s);
+    default: return dispatch_store<kBN, WBK_EPI_BIAS_MAXKEY, kPair>(tma, m, p, grid, s);
   }
+}
+
+// 3-D view of a row-major [rows, K] fp8 matrix as (128 bytes of K, rows, K / 128 blocks)
+// with a box of (128, box_rows, g): one load brings g consecutive K blocks, each a
+// [box_rows x 128 B] 128-byte-swizzled block, stacked in shared memory. Needs K % 128 == 0
+// (a partial last block would read past the row end instead of zero-filling).
+int make_tmap_kblocks(CUtensorMap* map, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows, uint32_t g) {
+  auto encode = get_encode_fn();
+  if (encode == nullptr) return fail(WBK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(BK), rows, K / BK};
+  const cuuint64_t strides[2] = {K, static_cast<cuuint64_t>(BK)};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(BK), box_rows, g};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(WBK_ERR_CUDA, "cuTensorMapEncodeTiled (K blocks) failed (%d)", static_cast<int>(r));
+  return WBK_OK;
+}
+
+// One 3-D TMA load per operand per stage (default on; WBK_GEMM_GROUPED=0 issues
+// the stage's K blocks as separate 2-D loads).
+bool kblocks_grouping_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_GEMM_GROUPED");
+    return !(e && e[0] == '0');
+  }();
+  return on;
 }
 
 bool pair_enabled() {
@@ -851,7 +919,10 @@ int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t 
   // TMA store and vector loads need 16-byte aligned rows: N % 8 == 0 and aligned bases.
   const bool vec = (N % 8 == 0) && aligned(out, 16) && (!bias || aligned(bias, 16)) && (!residual || aligned(residual, 16));
 
-  CUtensorMap ta, tw, to;
+  Maps maps;
+  CUtensorMap& ta = maps.a;
+  CUtensorMap& tw = maps.w;
+  CUtensorMap& to = maps.out;
   // M <= 64 (decoder step): load a 64-row A box; the MMA still reads 128 rows, and
   // TMEM lanes 64..127 (computed from stale shared memory) are never stored.
   const uint32_t a_box_rows = M <= 64 ? 64u : static_cast<uint32_t>(BM);
@@ -869,6 +940,20 @@ int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t 
       return e;
   } else {
     to = ta;  // unused by the direct-store kernel
+  }
+  // One 3-D load per operand per stage when K is a whole number of 128-byte blocks.
+  const int group = bn == 64 ? Tile<64>::G : (pair ? Tile<256, true>::G : Tile<128>::G);
+  bool grouped = K % BK == 0 && kblocks_grouping_enabled();
+  if (grouped) {
+    // If the driver does not take the blocked view, fall back to per-block 2-D loads.
+    grouped = make_tmap_kblocks(&maps.a3, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), a_box_rows,
+                                static_cast<uint32_t>(group)) == WBK_OK &&
+              make_tmap_kblocks(&maps.w3, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), w_box_rows,
+                                static_cast<uint32_t>(group)) == WBK_OK;
+  }
+  if (!grouped) {
+    maps.a3 = ta;  // unused: the kernel issues per-block 2-D loads
+    maps.w3 = tw;
   }
 
   Params p;
@@ -910,6 +995,7 @@ int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t 
   p.out_amax = out_amax_bits;
   p.out_pairs = (N % 2 == 0) && aligned(out, 4);
   p.a_box_bytes = a_box_rows * BK;
+  p.grouped = grouped ? 1 : 0;
   // Instruction descriptor (kind::f8f6f4): D fp32 [4,6)=1; A format [7,10);
   // B format [10,13); both K-major (bits 15,16 = 0); N>>3 [17,23); M>>4 [24,29).
   p.idesc = (1u << 4) | (static_cast<uint32_t>(a_fmt) << 7) | (static_cast<uint32_t>(w_fmt) << 10) |
@@ -920,12 +1006,12 @@ int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t 
   if (pair) {
     const int pairs = sms / 2;
     const int grid = 2 * static_cast<int>(num_tiles < pairs ? num_tiles : pairs);
-    return dispatch_epi<256, true>(epilogue, vec, ta, tw, to, p, grid, s);
+    return dispatch_epi<256, true>(epilogue, vec, maps, p, grid, s);
   }
   const int grid = p.num_items < sms ? p.num_items : sms;
-  if (bn == 64) return dispatch_epi<64>(epilogue, vec, ta, tw, to, p, grid, s);
-  if (bn == 128) return dispatch_epi<128>(epilogue, vec, ta, tw, to, p, grid, s);
-  return dispatch_epi<256>(epilogue, vec, ta, tw, to, p, grid, s);
+  if (bn == 64) return dispatch_epi<64>(epilogue, vec, maps, p, grid, s);
+  if (bn == 128) return dispatch_epi<128>(epilogue, vec, maps, p, grid, s);
+  return dispatch_epi<256>(epilogue, vec, maps, p, grid, s);
 }
 
 int wbk_device_error(uint32_t* code_out) {
