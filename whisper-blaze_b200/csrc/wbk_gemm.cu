@@ -36,6 +36,7 @@
 
 #include <cstdlib>
 #include <mutex>
+#include <string>
 #include <vector>
 
 #include "wbk_common.cuh"
@@ -852,17 +853,31 @@ constexpr int kMaxSplitTiles = 512;
 // ~7 % faster); at M = 64 the fp32 partial round trip costs more than the
 // shorter K loop saves (N = 1280, K = 5120: 24.6 us split vs 17.7 us), so the
 // plan is 1 there.
+// WBK_SPLITK = auto (default: the measured rule above) | off | max (split whenever
+// the tiles leave half the SMs idle, one stage per slice at least; for tuning).
+int splitk_mode() {
+  static const int mode = [] {
+    const char* e = std::getenv("WBK_SPLITK");
+    if (e == nullptr) return 0;
+    const std::string v(e);
+    return v == "off" ? 1 : (v == "max" ? 2 : 0);
+  }();
+  return mode;
+}
+
 void splitk_plan(int64_t M, int64_t N, int64_t K, int* splits, int* tiles) {
   *splits = 1;
   *tiles = 0;
-  if (M <= 0 || N <= 0 || K <= 0 || M > 32) return;
+  const int mode = splitk_mode();
+  if (M <= 0 || N <= 0 || K <= 0 || M > (mode == 2 ? BM : 32) || mode == 1) return;
   const int sms = sm_count() > 0 ? sm_count() : 148;
   const int64_t t = (N + 63) / 64;
   const int64_t kblocks = (K + BK - 1) / BK;
+  const int64_t stages = (kblocks + Tile<64>::G - 1) / Tile<64>::G;
   *tiles = static_cast<int>(t);
-  if (2 * t > sms || t > kMaxSplitTiles || kblocks < 16) return;
+  if (2 * t > sms || t > kMaxSplitTiles || (mode == 0 && kblocks < 16)) return;
   int64_t sp = sms / t;
-  if (sp > kblocks / 4) sp = kblocks / 4;
+  if (sp > stages) sp = stages;
   if (sp > 16) sp = 16;
   *splits = static_cast<int>(sp < 1 ? 1 : sp);
 }
