@@ -135,3 +135,20 @@ def test_graphed_forward_matches_eager(cuda_device, attention):
     assert torch.equal(y1, y_eager) and torch.equal(y2, y_eager)
     y_host = stack.forward_host(h.cpu().pin_memory(), graphed=True)
     assert torch.equal(y_host, y_eager.cpu())
+
+
+def test_forward_host_stream_matches_forward(cuda_device):
+    """The pipelined host API (copy-in / compute / copy-out overlapped through two buffer
+    pairs) returns, batch by batch, exactly what forward() returns on the same input."""
+    cfg = EncoderConfig(layers=2, seq_len=64)
+    stack = FP8EncoderStack(cfg, _layers(cfg, 2, 21), cuda_device)
+    batches = [randn_f16((3, 64, cfg.d_model), 30 + i).pin_memory() for i in range(5)]
+    outs = [torch.empty(b.shape, dtype=torch.float16).pin_memory() for b in batches]
+    stack.forward_host_stream(batches, outs)
+    torch.cuda.synchronize()
+    for b, o in zip(batches, outs):
+        assert torch.equal(o, stack.forward(b.to(cuda_device)).cpu())
+    # None entries skip the copy-out; a second call reuses the buffers and graphs
+    stack.forward_host_stream(batches[:2], [None, outs[0]])
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], stack.forward(batches[1].to(cuda_device)).cpu())

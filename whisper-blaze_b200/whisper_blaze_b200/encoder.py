@@ -27,7 +27,7 @@ from __future__ import annotations
 
 import os
 from dataclasses import dataclass, field
-from typing import Callable, List, Optional
+from typing import Callable, List, Optional, Sequence
 
 import torch
 import torch.nn.functional as F
@@ -165,16 +165,16 @@ class FP8EncoderStack:
             self.final_b = final_ln[1].to(self.device)
         self._ws_tokens = -1
         self.gemm_timings: Optional[List[GemmTiming]] = None  # set to [] to record
-        self._graph = None
-        self._graph_key = None
         self.launches_per_forward: Optional[int] = None  # libwbk launches of the last eager forward
-        self._graph_out = None
+        self._graphs: dict = {}  # (input, shape, device, output) -> (CUDA graph, output tensor)
+        self._stream_state = None
         self._host_in = None
 
     # -------------------------------------------------------------- buffers
     def _workspace(self, T: int) -> None:
         if self._ws_tokens == T:
             return
+        self._graphs.clear()  # captured graphs point into the buffers being replaced
         D, Fd, dev = self.cfg.d_model, self.cfg.ffn, self.device
         e = lambda *s, dt=torch.float16: torch.empty(*s, dtype=dt, device=dev)  # noqa: E731
         self.h_a, self.h_b, self.h2 = e(T, D), e(T, D), e(T, D)
@@ -300,26 +300,84 @@ class FP8EncoderStack:
         return o_full.view(B, S, D)
 
     @torch.inference_mode()
-    def forward_graphed(self, hidden: torch.Tensor) -> torch.Tensor:
+    def forward_graphed(self, hidden: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """forward() replayed from a CUDA graph: the ~36 launches per layer cost one
-        graph launch. The graph is captured on the first call for a given input
-        tensor (address and shape) and replayed on later calls with the same
-        tensor; the returned output lives in the graph's memory and is
-        overwritten by the next replay."""
+        graph launch. A graph is captured on the first call for a given (input,
+        output) pair of tensors (addresses and shape) and replayed on later calls
+        with the same tensors; with out=None the result lives in the stack's own
+        output buffer and is overwritten by the next replay."""
         ops.require_input(hidden, "hidden")
-        key = (hidden.data_ptr(), tuple(hidden.shape), hidden.device)
-        if self._graph is None or self._graph_key != key:
-            self._graph = None
+        key = (hidden.data_ptr(), tuple(hidden.shape), hidden.device, None if out is None else out.data_ptr())
+        entry = self._graphs.get(key)
+        if entry is None:
             with torch.cuda.device(self.device):
-                self.forward(hidden)  # sizes the workspace and runs every lazy initialisation
+                self.forward(hidden, out=out)  # sizes the workspace and runs every lazy initialisation
                 torch.cuda.synchronize(self.device)
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):
-                    y = self.forward(hidden)
+                    y = self.forward(hidden, out=out)
                 torch.cuda.synchronize(self.device)
-            self._graph, self._graph_key, self._graph_out = g, key, y
-        self._graph.replay()
-        return self._graph_out
+            entry = (g, y)
+            self._graphs[key] = entry
+        entry[0].replay()
+        return entry[1]
+
+    @torch.inference_mode()
+    def forward_host_stream(self, host_inputs: Sequence[torch.Tensor],
+                            host_outputs: Sequence[Optional[torch.Tensor]],
+                            post: Optional[Callable[[torch.Tensor], torch.Tensor]] = None) -> None:
+        """Pipelined host-to-host inference over a sequence of pinned batches.
+
+        Batch i's host->device copy runs on one copy stream and batch i-1's
+        device->host copy on another while batch i-1 / i compute (graphed)
+        on the current stream, through two device input and two device output
+        buffers ordered by events; `post` (e.g. an all-gather of the sharded
+        outputs) runs on the current stream after each forward and its result
+        is what lands in host_outputs[i] (None entries skip the copy-out).
+        Returns with every copy enqueued
+        before the current stream's next work (the caller synchronises)."""
+        if len(host_inputs) != len(host_outputs):
+            raise ValueError("host_inputs and host_outputs must have the same length")
+        if not host_inputs:
+            return
+        shape = tuple(host_inputs[0].shape)
+        dev = self.device
+        cs = torch.cuda.current_stream(dev)
+        if self._stream_state is None or self._stream_state["shape"] != shape:
+            e = lambda: torch.empty(shape, dtype=torch.float16, device=dev)  # noqa: E731
+            self._stream_state = {"shape": shape, "in": [e(), e()], "out": [e(), e()],
+                                  "h2d": torch.cuda.Stream(dev), "d2h": torch.cuda.Stream(dev)}
+        st = self._stream_state
+        h2d_s, d2h_s = st["h2d"], st["d2h"]
+        ev_h2d = [torch.cuda.Event() for _ in range(2)]
+        ev_comp = [torch.cuda.Event() for _ in range(2)]
+        ev_d2h = [torch.cuda.Event() for _ in range(2)]
+        with torch.cuda.device(dev):
+            # the buffers may still be read or written by work queued before this call
+            h2d_s.wait_stream(cs)
+            d2h_s.wait_stream(cs)
+            for i, (hin, hout) in enumerate(zip(host_inputs, host_outputs)):
+                b = i % 2
+                with torch.cuda.stream(h2d_s):
+                    if i >= 2:
+                        h2d_s.wait_event(ev_comp[b])  # forward i-2 has finished reading in[b]
+                    st["in"][b].copy_(hin, non_blocking=True)
+                    ev_h2d[b].record(h2d_s)
+                cs.wait_event(ev_h2d[b])
+                if i >= 2:
+                    cs.wait_event(ev_d2h[b])  # copy-out of i-2 has finished reading out[b]
+                y = self.forward_graphed(st["in"][b], out=st["out"][b])
+                res = post(y) if post is not None else y
+                ev_comp[b].record(cs)
+                with torch.cuda.stream(d2h_s):
+                    d2h_s.wait_event(ev_comp[b])
+                    if hout is not None:  # None: this rank keeps no host copy
+                        hout.copy_(res, non_blocking=True)
+                    ev_d2h[b].record(d2h_s)
+                if res is not y:
+                    res.record_stream(d2h_s)
+            cs.wait_stream(d2h_s)
+            cs.wait_stream(h2d_s)
 
     def device_input(self, hidden_host: torch.Tensor) -> torch.Tensor:
         """Copy a (pinned) host batch into this stack's persistent device input buffer
