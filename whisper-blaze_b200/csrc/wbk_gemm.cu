@@ -134,9 +134,14 @@ struct Params {
 // K blocks [kb0, kb1) of split `split`, whole stages of g blocks (every split
 // gets at least one stage when splits <= stages).
 __device__ __forceinline__ void split_range(const Params& p, int g, int split, int& kb0, int& kb1) {
-  const int64_t nst = (p.kblocks + g - 1) / g;
-  kb0 = static_cast<int>(static_cast<int64_t>(split) * nst / p.splits) * g;
-  kb1 = static_cast<int>(static_cast<int64_t>(split + 1) * nst / p.splits) * g;
+  if (p.splits == 1) {  // the common case, without integer division on the critical path
+    kb0 = 0;
+    kb1 = p.kblocks;
+    return;
+  }
+  const int nst = (p.kblocks + g - 1) / g;  // < 2^24 stages and <= 16 splits: 32-bit products suffice
+  kb0 = (split * nst / p.splits) * g;
+  kb1 = ((split + 1) * nst / p.splits) * g;
   if (kb1 > p.kblocks) kb1 = p.kblocks;
 }
 
@@ -190,16 +195,17 @@ __device__ __forceinline__ void prefetch_residual(const Params& p, int row, int 
 // fp32 accumulators of one 32-column chunk of this thread's row -> epilogue
 // values in fp32 (descale, bias, activation, residual, clamp). Columns >= N
 // and rows >= M are never read from global memory.
+// bias_pre: the chunk's 32 bias values already loaded into registers (nullptr: load them).
 template <int kEpi, bool kVec>
 __device__ __forceinline__ void epi_values(const Params& p, const uint32_t* acc, const uint4* res, int row, int col0,
-                                           float descale, float* v) {
+                                           float descale, float* v, const uint4* bias_pre = nullptr) {
   const int N = p.N;
   const bool full = kVec && (col0 + 32 <= N);
   if (p.bias != nullptr && full) {
     const uint4* bv = reinterpret_cast<const uint4*>(p.bias + col0);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const uint4 b = __ldg(bv + q);
+      const uint4 b = bias_pre != nullptr ? bias_pre[q] : __ldg(bv + q);
       const __half2* h = reinterpret_cast<const __half2*>(&b);
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
@@ -487,6 +493,14 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       const int row = row0 + lane;
       uint4 resa[4], resb[4];
       prefetch_residual<kEpi, kTmaStore>(p, row, n0, resa);  // overlaps the tile's MMAs
+      // 64-wide tiles (one 32-column chunk per warp): the bias is loaded before the
+      // accumulator wait too, off the short-M GEMMs' critical path.
+      uint4 bpre[4];
+      const bool bias_early = kBN == 64 && kTmaStore && p.bias != nullptr && n0 + CHUNK <= p.N;
+      if (bias_early) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) bpre[q] = __ldg(reinterpret_cast<const uint4*>(p.bias + n0) + q);
+      }
       if (!mbar_wait(&s.acc_full[acc], acc_phase, abort_flag, p.timeout_ns, SITE_EPI_ACC_FULL)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -495,7 +509,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       auto process = [&](const uint32_t* regs, const uint4* res, int c) {
         const int col0 = n0 + c * CHUNK;
         float v[32];
-        epi_values<kEpi, kTmaStore>(p, regs, res, row, col0, descale, v);
+        epi_values<kEpi, kTmaStore>(p, regs, res, row, col0, descale, v, (bias_early && c == 0) ? bpre : nullptr);
         const int valid_cols = (row < p.M) ? min(CHUNK, p.N - col0) : 0;
         amax = kSignedMax ? max_valid(amax, v, valid_cols) : absmax_valid(amax, v, valid_cols);
         uint32_t w[16];
@@ -644,7 +658,9 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         acc_phase ^= 1u;
       }
     }
-    if (kTmaStore && lane == 0) bulk_wait_all();  // all of this warp's stores have landed
+    // The staging buffers must have been read before the CTA exits; the global
+    // writes themselves complete with the grid.
+    if (kTmaStore && lane == 0) bulk_wait_read<0>();
     if (p.out_amax != nullptr) {
       const uint32_t h = __half_as_ushort(__float2half_rn(amax));
       const uint32_t bits = warp_max_u32(kSignedMax ? f16_order_key(h) : h);
