@@ -221,10 +221,10 @@ def test_quantise_gelu_negative_side_amax(cuda_device):
     assert abs(s.item() * 448.0 - g.abs().max().item()) <= 2e-3 * g.abs().max().item()
 
 
-@pytest.mark.parametrize("n", [1, 4099, 81920, 262144, 262145])
+@pytest.mark.parametrize("n", [1, 8, 4099, 8192, 81920, 81928, 262144, 262145])
 def test_small_tensor_path_matches_two_kernel_path(cuda_device, n):
-    """wbk_quantise_f16 takes a single-CTA path up to 262144 elements; it must give the bytes and scale
-    of the amax kernel + quantise kernel pair."""
+    """wbk_quantise_f16 takes a single-CTA path up to 262144 elements (register-resident up to 81920,
+    n % 8 == 0); it must give the bytes and scale of the amax kernel + quantise kernel pair."""
     x = randn_f16((n,), 400 + n % 97, std=3.0).to(cuda_device)
     q, s = ops.quantise(x)
     ws = ops.new_amax_ws(cuda_device)

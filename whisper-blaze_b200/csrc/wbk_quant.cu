@@ -359,6 +359,58 @@ quantise_small_kernel(const __half* __restrict__ x, int64_t n, float max_fp8, ui
   }
 }
 
+// Register-resident variant for the smallest tensors (decoder-step activations,
+// n <= 1024 threads x 10 x 8 elements): every thread issues all its 16-byte
+// loads at once and keeps them in registers, so the tensor crosses memory once
+// (one round trip of latency) instead of twice; same codes and scale.
+constexpr int kRegVecs = 10;
+constexpr int64_t kRegQuantMax = static_cast<int64_t>(kSmallThreads) * kRegVecs * 8;
+
+template <int kFmt>
+__global__ void __launch_bounds__(kSmallThreads, 1)
+quantise_regs_kernel(const __half* __restrict__ x, int64_t n, float max_fp8, uint8_t* __restrict__ q,
+                     float* __restrict__ scale_out, uint32_t* __restrict__ amax_out) {
+  griddep_launch_dependents();  // a following GEMM may run its prologue meanwhile
+  __shared__ uint32_t red[kSmallThreads / 32];
+  __shared__ float sc[2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nvec = static_cast<int>(n >> 3);
+  const uint4* xv = reinterpret_cast<const uint4*>(x);
+  uint4 v[kRegVecs];
+#pragma unroll
+  for (int k = 0; k < kRegVecs; ++k) {
+    const int i = threadIdx.x + k * kSmallThreads;
+    v[k] = i < nvec ? ld_stream16(xv + i) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  uint32_t m = 0;
+#pragma unroll
+  for (int k = 0; k < kRegVecs; ++k)
+    m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v[k].x), abs2_nonan(v[k].y)),
+                             __vmaxu2(abs2_nonan(v[k].z), abs2_nonan(v[k].w))));
+  uint32_t mm = warp_max_u32(max(m & 0xFFFFu, m >> 16));
+  if (lane == 0) red[warp] = mm;
+  __syncthreads();
+  if (warp == 0) {
+    mm = warp_max_u32(red[lane]);
+    if (lane == 0) {
+      float scale, inv;
+      scale_from_amax(mm, max_fp8, scale, inv);
+      sc[0] = scale;
+      sc[1] = inv;
+      if (scale_out != nullptr) *scale_out = scale;
+      if (amax_out != nullptr) *amax_out = mm;
+    }
+  }
+  __syncthreads();
+  const float inv = sc[1];
+  uint2* qv = reinterpret_cast<uint2*>(q);
+#pragma unroll
+  for (int k = 0; k < kRegVecs; ++k) {
+    const int i = threadIdx.x + k * kSmallThreads;
+    if (i < nvec) qv[i] = make_uint2(q8x4<kFmt>(v[k].x, v[k].y, inv, max_fp8), q8x4<kFmt>(v[k].z, v[k].w, inv, max_fp8));
+  }
+}
+
 // -------------------------------------------------------------- dequantise
 
 template <int kFmt>
@@ -547,6 +599,11 @@ int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out, float* scal
     const __half* xh = static_cast<const __half*>(x);
     uint8_t* q = static_cast<uint8_t*>(q_out);
     const float mx = fmt_max(fmt);
+    if (vec && n % 8 == 0 && n <= kRegQuantMax) {
+      if (fmt == WBK_FMT_E4M3) quantise_regs_kernel<WBK_FMT_E4M3><<<1, kSmallThreads, 0, s>>>(xh, n, mx, q, scale_out, amax_ws);
+      else quantise_regs_kernel<WBK_FMT_E5M2><<<1, kSmallThreads, 0, s>>>(xh, n, mx, q, scale_out, amax_ws);
+      return cuda_check(cudaGetLastError(), "wbk_quantise_f16 (small, registers) launch");
+    }
     if (fmt == WBK_FMT_E4M3) {
       if (vec) quantise_small_kernel<WBK_FMT_E4M3, true><<<1, kSmallThreads, 0, s>>>(xh, n, mx, q, scale_out, amax_ws);
       else quantise_small_kernel<WBK_FMT_E4M3, false><<<1, kSmallThreads, 0, s>>>(xh, n, mx, q, scale_out, amax_ws);
