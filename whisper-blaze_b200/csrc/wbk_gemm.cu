@@ -849,13 +849,28 @@ bool pair_enabled() {
   return on;
 }
 
-// Tile width: 256 unless that leaves SMs idle. Short-M GEMMs (the decoder step)
-// are weight-streaming, HBM-bound: narrow tiles spread the weight over every SM.
+// Tile width. Short-M GEMMs (the decoder step) are weight-streaming and
+// HBM-bound: 64-wide tiles spread the weight over every SM. Otherwise the
+// choice is 256-wide tiles on CTA pairs or 128-wide tiles on single CTAs, by
+// rounds of tiles: measured on B200, a CTA computing a 128 x 128 tile does
+// ~0.63 of the work of a pair round (256 x 256 on two SMs) in the same time
+// per SM — the pair halves each SM's operand traffic per FLOP, which is what
+// limits it — so pairs win unless they leave too many SMs idle in their last
+// round (1500 x 5120 x 1280: 2 pair rounds beat 4 single-CTA rounds by 11 %).
 int pick_bn(int64_t M, int64_t N, int sms) {
-  const int64_t tiles_m = (M + BM - 1) / BM;
+  static const int forced = [] {  // WBK_GEMM_BN=64|128|256 overrides the choice for M > 128 (tuning)
+    const char* e = std::getenv("WBK_GEMM_BN");
+    const int v = e ? std::atoi(e) : 0;
+    return (v == 64 || v == 128 || v == 256) ? v : 0;
+  }();
   if (M <= BM) return 64;
-  if (tiles_m * ((N + 255) / 256) >= 2 * sms) return 256;
-  return 128;
+  if (forced) return forced;
+  const int64_t pairs = sms / 2 > 0 ? sms / 2 : 1;
+  const int64_t pair_tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+  const int64_t single_tiles = ((M + BM - 1) / BM) * ((N + 127) / 128);
+  const int64_t pair_rounds = (pair_tiles + pairs - 1) / pairs;
+  const int64_t single_rounds = (single_tiles + sms - 1) / sms;
+  return 100 * pair_rounds <= 65 * single_rounds ? 256 : 128;
 }
 
 // The ticket block has one fixed size for every shape (split-K needs 2 * tiles <= SMs,
