@@ -242,8 +242,28 @@ int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t 
                     int epilogue, uint32_t* out_amax_bits,
                     void* workspace, int64_t workspace_bytes, wbk_stream_t stream);
 
-/* Bytes of split-K workspace wbk_gemm_fp8_ws uses for this shape (0: none). */
+/* Bytes of workspace wbk_gemm_fp8_ws (split-K) and wbk_linear_fp8_f16 (its
+ * in-kernel quantise) use for this shape (0: none). */
 int64_t wbk_gemm_fp8_ws_bytes(int64_t M, int64_t N, int64_t K);
+
+/* FP8 linear on an fp16 activation: quantises A16 [M, K] per tensor exactly as
+ * wbk_quantise_f16 (codes into a_q_out, scale into *a_scale_out, amax bits into
+ * *a_amax_ws), then out = wbk_gemm_fp8_ws(codes, W, ...) with that scale.
+ * Replaces the pair of calls BlazeLinear.forward makes per FP8 linear
+ * (quantise_e4m3 then the scaled GEMM, whisper_blaze/model.py:80-109).
+ * For 0 < M <= 128 with 16-byte aligned A16 / a_q_out and a workspace
+ * (wbk_gemm_fp8_ws_bytes(M, N, K) bytes, zero-filled before first use, not used
+ * by two calls at once) it is ONE cooperative kernel: the GEMM's CTAs quantise
+ * A together (grid-wide amax, then codes) before their tiles, so the short-M
+ * decoder-step linears launch one kernel instead of two. Otherwise it is the two
+ * launches. Codes, scale, amax bits and output are identical either way. After
+ * a WBK_ERR_DEVICE_TIMEOUT the workspace must be zero-filled again. */
+int wbk_linear_fp8_f16(const void* A16, int64_t M, int64_t N, int64_t K, int a_fmt,
+                       void* a_q_out, float* a_scale_out, uint32_t* a_amax_ws,
+                       const void* W, int w_fmt, const float* w_scale, float alpha,
+                       const void* bias, const void* residual, void* out,
+                       int epilogue, uint32_t* out_amax_bits,
+                       void* workspace, int64_t workspace_bytes, wbk_stream_t stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -178,8 +178,8 @@ def test_gemm_split_k(cuda_device, M, N, K, epi):
         from oracle.gemm import order_key_f16
         assert key.item() == order_key_f16(float(y1.float().max()))
     if need > 0:
-        # the ticket block (first 16 KB of the workspace) must be all zero again
-        assert int(ws[:16384].view(torch.int32).abs().sum().item()) == 0
+        # the sync words and the ticket block (first 256 B + 16 KB of the workspace) must be all zero again
+        assert int(ws[:256 + 16384].view(torch.int32).abs().sum().item()) == 0
     assert _lib.device_error() == 0
 
 
@@ -188,9 +188,10 @@ def test_gemm_split_k_workspace_errors(cuda_device):
     M, N, K = 16, 1280, 5120
     need = _lib.lib().wbk_gemm_fp8_ws_bytes(M, N, K)
     assert need > 0
-    assert _lib.lib().wbk_gemm_fp8_ws_bytes(4096, 1280, 1280) == 0  # large M: no split
-    assert _lib.lib().wbk_gemm_fp8_ws_bytes(16, 1280, 1280) == 0  # short K: no split
-    assert _lib.lib().wbk_gemm_fp8_ws_bytes(64, 1280, 5120) == 0  # M = 64: no split
+    assert _lib.lib().wbk_gemm_fp8_ws_bytes(4096, 1280, 1280) == 0  # large M: no split, no in-kernel quantise
+    # M <= 128 without a split: only the in-kernel quantise's sync words (wbk_linear_fp8_f16)
+    assert _lib.lib().wbk_gemm_fp8_ws_bytes(16, 1280, 1280) == 256  # short K: no split
+    assert _lib.lib().wbk_gemm_fp8_ws_bytes(64, 1280, 5120) == 256  # M = 64: no split
     aq, sa, wq, sw, b = _operands(M, N, K, 5, cuda_device)
     small = torch.zeros(need // 2, dtype=torch.uint8, device=cuda_device)
     with pytest.raises(RuntimeError, match="workspace"):

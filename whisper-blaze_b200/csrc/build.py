@@ -5,9 +5,10 @@
 Objects go to whisper-blaze_b200/_build/, the library to
 whisper-blaze_b200/lib/libwbk.so. The CUDA runtime is linked statically so the
 library does not depend on which libcudart the host process loaded first.
-The quantiser unit is compiled with --use_fast_math, matching the reference's
-own quantiser build (setup.py:41-54), so that its scale division is the same
-compiler division; every other unit uses IEEE defaults.
+The quantiser unit is compiled with --use_fast_math, the flag set of the
+reference's own quantiser build (setup.py:41-54); its scale division is the
+explicit approximate quotient of wbk_fp8_quant.cuh, which the GEMM unit (IEEE
+defaults, like every other unit) shares.
 """
 from __future__ import annotations
 
@@ -37,7 +38,8 @@ UNITS = {
     "wbk_gemm.cu": [],
     "wbk_attn.cu": [],
 }
-HEADERS = [os.path.join(HERE, "wbk_common.cuh"), os.path.join(HERE, "wbk_sm100.cuh"), os.path.join(INCLUDE, "wbk.h")]
+HEADERS = [os.path.join(HERE, "wbk_common.cuh"), os.path.join(HERE, "wbk_sm100.cuh"),
+           os.path.join(HERE, "wbk_fp8_quant.cuh"), os.path.join(INCLUDE, "wbk.h")]
 
 
 def nvcc() -> str:

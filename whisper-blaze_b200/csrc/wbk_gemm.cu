@@ -37,9 +37,11 @@
 #include <cstdlib>
 #include <mutex>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "wbk_common.cuh"
+#include "wbk_fp8_quant.cuh"
 #include "wbk_sm100.cuh"
 
 namespace wbk {
@@ -87,6 +89,7 @@ enum : uint32_t {
   SITE_MMA_FULL = 3,
   SITE_EPI_ACC_FULL = 4,
   SITE_DRAIN = 5,
+  SITE_QUANT_SYNC = 6,
   SITE_SELFTEST = 15,
 };
 
@@ -102,6 +105,11 @@ struct SharedStorage {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
+  // in-kernel activation quantise (short-M linear): per-warp amax, the scale, status
+  uint32_t qred[THREADS / 32];
+  uint32_t qamax;
+  float qscale, qinv;
+  int qok;
 };
 template <int kBN, bool kPair = false>
 constexpr size_t smem_bytes() { return sizeof(SharedStorage<kBN, kPair>) + 1024; }
@@ -131,6 +139,23 @@ struct Params {
   uint32_t* ws_tickets;   // [num_tiles][EPI_WARPS] arrival counts, zero between calls
 };
 
+// Parameters of the in-kernel activation quantise (64-wide tiles, cooperative
+// launch): A is quantised per tensor from a_f16 into a_q, which the TMA then
+// reads as A. Only those kernels take the larger block (ptxas allocates the
+// other kernels' registers differently when their parameter block grows).
+struct QuantParams : Params {
+  const __half* a_f16;    // [M, K] fp16, rows contiguous
+  uint8_t* a_q;           // [M, K] fp8 codes (out)
+  float* a_scale_out;     // the quantiser's scale (out, may be null)
+  uint32_t* a_amax_out;   // the quantiser's amax bits (out, may be null)
+  uint32_t* qsync;        // 4 workspace words: arrivals (amax), arrivals (codes), departures, amax; zero between calls
+  int64_t a_vecs;         // M * K / 8 (16-byte vectors of A)
+  float a_max_fp8;
+  int a_e5m2;
+};
+template <bool kQuantA>
+using KernelParams = typename std::conditional<kQuantA, QuantParams, Params>::type;
+
 // K blocks [kb0, kb1) of split `split`, whole stages of g blocks (every split
 // gets at least one stage when splits <= stages).
 __device__ __forceinline__ void split_range(const Params& p, int g, int split, int& kb0, int& kb1) {
@@ -145,6 +170,32 @@ __device__ __forceinline__ void split_range(const Params& p, int g, int split, i
   if (kb1 > p.kblocks) kb1 = p.kblocks;
 }
 
+// Grid-wide arrival for the cooperatively launched (all CTAs co-resident)
+// in-kernel quantise: publishes this CTA's earlier global writes, counts it in
+// *count, and waits until all `expected` CTAs have arrived. Bounded: gives up
+// after `timeout_ns` of wall clock, recording the error.
+__device__ __noinline__ bool grid_arrive_wait(uint32_t* count, uint32_t expected, uint64_t timeout_ns) {
+  __threadfence();
+  atomicAdd(count, 1u);
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0; it < (1u << 30); ++it) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(count) : "memory");
+    if (v >= expected) return true;
+    if ((it & 15u) == 15u && globaltimer_ns() - t0 > timeout_ns) break;
+  }
+  record_device_error(WBK_ERR_DEVICE_TIMEOUT, SITE_QUANT_SYNC);
+  return false;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Generic-proxy global writes <-> async-proxy (TMA) reads of the same bytes.
+__device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // ----------------------------------------------------------------- epilogue
 
@@ -277,11 +328,11 @@ __device__ __forceinline__ float absmax_valid(float m, const float* v, int valid
 
 // ------------------------------------------------------------------- kernel
 
-template <int kBN, int kEpi, bool kTmaStore, bool kPair>
+template <int kBN, int kEpi, bool kTmaStore, bool kPair, bool kQuantA>
 __global__ void __launch_bounds__(THREADS, 1)
 fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                 const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_a3,
-                const __grid_constant__ CUtensorMap tmap_w3, const Params p) {
+                const __grid_constant__ CUtensorMap tmap_w3, const KernelParams<kQuantA> p) {
   extern __shared__ uint8_t smem_raw[];
   SharedStorage<kBN, kPair>& s =
       *reinterpret_cast<SharedStorage<kBN, kPair>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -334,12 +385,121 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
   // the kernel that produces A / the scales; nothing below runs before it is done.
   griddep_wait();
 
-  if (warp == 0) {
+  // TMA loads of one single-CTA stage: the A and/or W boxes of K blocks [kb, kb + G).
+  auto load_stage = [&](int stage, int kb, int m0, int n0, bool load_a, bool load_w) {
+    if (p.grouped) {
+      if (load_a) tma_load_3d(&tmap_a3, &s.full[stage], s.a[stage], 0, m0, kb);
+      if (load_w) tma_load_3d(&tmap_w3, &s.full[stage], s.b[stage], 0, n0, kb);
+    } else {
+#pragma unroll
+      for (int g = 0; g < TL::G; ++g) {
+        if (load_a) tma_load_2d(&tmap_a, &s.full[stage], s.a[stage] + g * p.a_box_bytes, (kb + g) * BK, m0);
+        if (load_w) tma_load_2d(&tmap_w, &s.full[stage], s.b[stage] + g * TL::B_SUB_BYTES, (kb + g) * BK, n0);
+      }
+    }
+  };
+
+  // In-kernel quantise of A (short-M linear). The W boxes of the first stages
+  // go out first and stream in meanwhile. Then every CTA takes the amax of its
+  // slice of A, the grid agrees on the tensor's amax (one bounded grid-wide
+  // arrival; the launch is cooperative, so all CTAs are resident), each CTA
+  // writes its slice's codes, and after a second arrival the pipeline below
+  // TMA-loads A from those codes as usual. The last CTA through zeroes the
+  // sync words for the next call.
+  int pre = 0;  // stages whose W half was issued ahead of the quantise
+  bool run = true;
+  if constexpr (kQuantA) {
+    static_assert(!kPair, "the in-kernel quantise is for single-CTA tiles");
+    if (warp == 0 && lane == 0 && first_tile < p.num_items) {
+      const int tile = first_tile / p.splits;
+      int kb0, kb1;
+      split_range(p, TL::G, first_tile - tile * p.splits, kb0, kb1);
+      const int n0 = (tile % p.tiles_n) * kBN;
+      for (int kb = kb0; kb < kb1 && pre < TL::STAGES; kb += TL::G, ++pre) {
+        mbar_arrive_expect_tx(&s.full[pre], TL::G * (p.a_box_bytes + TL::B_SUB_BYTES));
+        load_stage(pre, kb, 0, n0, false, true);
+      }
+    }
+    const int64_t v0 = p.a_vecs * blockIdx.x / gridDim.x;
+    const int64_t v1 = p.a_vecs * (blockIdx.x + 1) / gridDim.x;
+    const uint4* src = reinterpret_cast<const uint4*>(p.a_f16);
+    uint32_t m = 0;
+    for (int64_t i = v0 + threadIdx.x; i < v1; i += THREADS) m = max(m, absmax8_bits(__ldcg(src + i)));
+    m = warp_max_u32(m);
+    if (lane == 0) s.qred[warp] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      uint32_t mm = 0;
+#pragma unroll
+      for (int w = 0; w < THREADS / 32; ++w) mm = max(mm, s.qred[w]);
+      if (mm != 0u) atomicMax(p.qsync + 3, mm);
+      const bool ok = grid_arrive_wait(p.qsync + 0, gridDim.x, p.timeout_ns);
+      const uint32_t amax = ok ? ld_acquire_gpu(p.qsync + 3) : 0u;
+      float sc, inv;
+      scale_from_amax(amax, p.a_max_fp8, sc, inv);
+      s.qamax = amax;
+      s.qscale = sc;
+      s.qinv = inv;
+      s.qok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    if (s.qok) {
+      const float inv = s.qinv, mx = p.a_max_fp8;
+      uint2* dst = reinterpret_cast<uint2*>(p.a_q);
+      for (int64_t i = v0 + threadIdx.x; i < v1; i += THREADS) {
+        const uint4 v = __ldcg(src + i);
+        dst[i] = p.a_e5m2 ? make_uint2(q8x4<WBK_FMT_E5M2>(v.x, v.y, inv, mx), q8x4<WBK_FMT_E5M2>(v.z, v.w, inv, mx))
+                          : make_uint2(q8x4<WBK_FMT_E4M3>(v.x, v.y, inv, mx), q8x4<WBK_FMT_E4M3>(v.z, v.w, inv, mx));
+      }
+      fence_async_global();  // the codes are read back by TMA (async proxy), in other CTAs too
+      __threadfence();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && s.qok) {
+      const bool ok = grid_arrive_wait(p.qsync + 1, gridDim.x, p.timeout_ns);
+      if (ok) {
+        if (blockIdx.x == 0) {
+          if (p.a_scale_out != nullptr) *p.a_scale_out = s.qscale;
+          if (p.a_amax_out != nullptr) *p.a_amax_out = s.qamax;
+        }
+        // Every CTA has passed both arrivals once the last one leaves: nothing reads the words again.
+        if (atomicAdd(p.qsync + 2, 1u) == gridDim.x - 1u) {
+          p.qsync[0] = 0u;
+          p.qsync[1] = 0u;
+          p.qsync[3] = 0u;
+          p.qsync[2] = 0u;
+        }
+      }
+      s.qok = ok ? 1 : 0;
+    }
+    __syncthreads();
+    run = s.qok != 0;
+  }
+
+  if constexpr (kQuantA) {
+    if (!run && warp == 0 && lane == 0 && pre > 0) {
+      // The quantise gave up (timeout recorded): complete and wait out the stages
+      // whose W boxes are in flight (A's bytes may be stale, nothing uses them).
+      const int tile = first_tile / p.splits;
+      int kb0, kb1;
+      split_range(p, TL::G, first_tile - tile * p.splits, kb0, kb1);
+      for (int i = 0; i < pre; ++i) load_stage(i, kb0 + i * TL::G, 0, 0, true, false);
+      for (int i = 0; i < pre; ++i) {
+        int dummy = 0;
+        mbar_wait(&s.full[i], 0, &dummy, 1000000ull, SITE_DRAIN);
+      }
+    }
+  }
+  if (!run) {
+    // nothing else runs: straight to the teardown
+  } else if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      int n_st = 0;  // stages issued so far; the first `pre` have their W half in flight already
+      if constexpr (kQuantA) fence_async_global();
       for (int item = first_tile; item < p.num_items && ok; item += tile_stride) {
         const int tile = item / p.splits;
         int kb0, kb1;
@@ -347,6 +507,16 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         const int m0 = (tile / p.tiles_n) * TL::ROWS + row_off;
         const int n0 = (tile % p.tiles_n) * kBN + static_cast<int>(rank) * TL::B_ROWS;
         for (int kb = kb0; kb < kb1; kb += TL::G) {
+          if constexpr (kQuantA) {
+            if (n_st++ < pre) {  // W issued ahead: only A is left
+              load_stage(stage, kb, m0, n0, true, false);
+              if (++stage == TL::STAGES) {
+                stage = 0;
+                phase ^= 1u;
+              }
+              continue;
+            }
+          }
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) {
             ok = false;
             break;
@@ -369,16 +539,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
             }
           } else {
             mbar_arrive_expect_tx(&s.full[stage], stage_bytes);
-            if (p.grouped) {
-              tma_load_3d(&tmap_a3, &s.full[stage], s.a[stage], 0, m0, kb);
-              tma_load_3d(&tmap_w3, &s.full[stage], s.b[stage], 0, n0, kb);
-            } else {
-#pragma unroll
-              for (int g = 0; g < TL::G; ++g) {
-                tma_load_2d(&tmap_a, &s.full[stage], s.a[stage] + g * p.a_box_bytes, (kb + g) * BK, m0);
-                tma_load_2d(&tmap_w, &s.full[stage], s.b[stage] + g * TL::B_SUB_BYTES, (kb + g) * BK, n0);
-              }
-            }
+            load_stage(stage, kb, m0, n0, true, true);
           }
           if (++stage == TL::STAGES) {
             stage = 0;
@@ -476,7 +637,8 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     const int ew = warp - 2;             // 0..7
     const int quarter = warp & 3;        // TMEM lanes this warp may access: 32*quarter ..
     const int col_half = ew >> 2;        // which 128 of the 256 accumulator columns
-    const float descale = p.alpha * (p.a_scale ? __ldg(p.a_scale) : 1.0f) * (p.w_scale ? __ldg(p.w_scale) : 1.0f);
+    const float a_sc = kQuantA ? s.qscale : (p.a_scale ? __ldg(p.a_scale) : 1.0f);
+    const float descale = p.alpha * a_sc * (p.w_scale ? __ldg(p.w_scale) : 1.0f);
     constexpr bool kSignedMax = (kEpi == WBK_EPI_BIAS_MAXKEY);
     float amax = kSignedMax ? -INFINITY : 0.0f;  // max |out|, or max out for the key epilogue
     int acc = 0;
@@ -720,15 +882,26 @@ bool pdl_enabled() {
   return on;
 }
 
-template <int kBN, int kEpi, bool kTma, bool kPair>
+// Programmatic dependent launch for the cooperative (in-kernel quantise)
+// variant too (default off; WBK_PDL_COOP=1 turns it on).
+bool pdl_coop_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_PDL_COOP");
+    return e != nullptr && std::atoi(e) != 0;
+  }();
+  return on;
+}
+
+template <int kBN, int kEpi, bool kTma, bool kPair, bool kQuantA>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const CUtensorMap& ta3,
-                const CUtensorMap& tw3, const Params& p, int grid, cudaStream_t stream) {
+                const CUtensorMap& tw3, const QuantParams& qp, int grid, cudaStream_t stream) {
+  const KernelParams<kQuantA>& p = qp;
   static std::mutex mu;
   static std::vector<char> configured;
   const int dev = current_device();
   if (dev < 0) return fail(WBK_ERR_CUDA, "no current CUDA device");
   constexpr size_t kSmem = smem_bytes<kBN, kPair>();
-  auto kernel = fp8_gemm_kernel<kBN, kEpi, kTma, kPair>;
+  auto kernel = fp8_gemm_kernel<kBN, kEpi, kTma, kPair, kQuantA>;
   {
     std::lock_guard<std::mutex> lock(mu);
     if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
@@ -745,11 +918,17 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
   cfg.blockDim = dim3(THREADS, 1, 1);
   cfg.dynamicSmemBytes = kSmem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[3];
   int nattr = 0;
-  if (pdl_enabled()) {  // the kernel waits (griddep_wait) before reading anything a predecessor writes
+  // the kernel waits (griddep_wait) before reading anything a predecessor writes
+  if (kQuantA ? pdl_coop_enabled() : pdl_enabled()) {
     attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+  }
+  if (kQuantA) {  // the CTAs wait for one another: all must be resident at once
+    attr[nattr].id = cudaLaunchAttributeCooperative;
+    attr[nattr].val.cooperative = 1;
     ++nattr;
   }
   if (!kPair) {
@@ -796,20 +975,21 @@ struct Maps {
   CUtensorMap a, w, out, a3, w3;
 };
 
-template <int kBN, int kEpi, bool kPair>
-int dispatch_store(bool tma, const Maps& m, const Params& p, int grid, cudaStream_t s) {
-  return tma ? launch_gemm<kBN, kEpi, true, kPair>(m.a, m.w, m.out, m.a3, m.w3, p, grid, s)
-             : launch_gemm<kBN, kEpi, false, kPair>(m.a, m.w, m.out, m.a3, m.w3, p, grid, s);
+template <int kBN, int kEpi, bool kPair, bool kQuantA>
+int dispatch_store(bool tma, const Maps& m, const QuantParams& p, int grid, cudaStream_t s) {
+  return tma ? launch_gemm<kBN, kEpi, true, kPair, kQuantA>(m.a, m.w, m.out, m.a3, m.w3, p, grid, s)
+             : launch_gemm<kBN, kEpi, false, kPair, kQuantA>(m.a, m.w, m.out, m.a3, m.w3, p, grid, s);
 }
 
-template <int kBN, bool kPair = false>
-int dispatch_epi(int epilogue, bool tma, const Maps& m, const Params& p, int grid, cudaStream_t s) {
+template <int kBN, bool kPair = false, bool kQuantA = false>
+int dispatch_epi(int epilogue, bool tma, const Maps& m, const QuantParams& p, int grid, cudaStream_t s) {
   switch (epilogue) {
-    case WBK_EPI_NONE: return dispatch_store<kBN, WBK_EPI_NONE, kPair>(tma, m, p, grid, s);
-    case WBK_EPI_GELU: return dispatch_store<kBN, WBK_EPI_GELU, kPair>(tma, m, p, grid, s);
-    case WBK_EPI_RESIDUAL: return dispatch_store<kBN, WBK_EPI_RESIDUAL, kPair>(tma, m, p, grid, s);
-    case WBK_EPI_RESIDUAL_CLAMP: return dispatch_store<kBN, WBK_EPI_RESIDUAL_CLAMP, kPair>(tma, m, p, grid, s);
-    default: return dispatch_store<kBN, WBK_EPI_BIAS_MAXKEY, kPair>(tma, m, p, grid, s);
+    case WBK_EPI_NONE: return dispatch_store<kBN, WBK_EPI_NONE, kPair, kQuantA>(tma, m, p, grid, s);
+    case WBK_EPI_GELU: return dispatch_store<kBN, WBK_EPI_GELU, kPair, kQuantA>(tma, m, p, grid, s);
+    case WBK_EPI_RESIDUAL: return dispatch_store<kBN, WBK_EPI_RESIDUAL, kPair, kQuantA>(tma, m, p, grid, s);
+    case WBK_EPI_RESIDUAL_CLAMP:
+      return dispatch_store<kBN, WBK_EPI_RESIDUAL_CLAMP, kPair, kQuantA>(tma, m, p, grid, s);
+    default: return dispatch_store<kBN, WBK_EPI_BIAS_MAXKEY, kPair, kQuantA>(tma, m, p, grid, s);
   }
 }
 
@@ -858,13 +1038,13 @@ bool pair_enabled() {
 // limits it — so pairs win unless they leave too many SMs idle in their last
 // round (1500 x 5120 x 1280: 2 pair rounds beat 4 single-CTA rounds by 11 %).
 int pick_bn(int64_t M, int64_t N, int sms) {
-  static const int forced = [] {  // WBK_GEMM_BN=64|128|256 overrides the choice for M > 128 (tuning)
+  static const int forced = [] {  // WBK_GEMM_BN=64|128|256 overrides the choice (tuning)
     const char* e = std::getenv("WBK_GEMM_BN");
     const int v = e ? std::atoi(e) : 0;
     return (v == 64 || v == 128 || v == 256) ? v : 0;
   }();
-  if (M <= BM) return 64;
   if (forced) return forced;
+  if (M <= BM) return 64;
   const int64_t pairs = sms / 2 > 0 ? sms / 2 : 1;
   const int64_t pair_tiles = ((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
   const int64_t single_tiles = ((M + BM - 1) / BM) * ((N + 127) / 128);
@@ -913,10 +1093,37 @@ void splitk_plan(int64_t M, int64_t N, int64_t K, int* splits, int* tiles) {
   *splits = static_cast<int>(sp < 1 ? 1 : sp);
 }
 int64_t splitk_ticket_bytes(int /*tiles*/) { return static_cast<int64_t>(kMaxSplitTiles) * EPI_WARPS * 4; }
+// Workspace layout: [kSyncBytes: the in-kernel quantise's sync words][split-K
+// tickets][split-K partials]; every word is back at zero when a call ends.
+constexpr int64_t kSyncBytes = 256;
 int64_t splitk_ws_bytes(int splits, int tiles) {
   if (splits <= 1) return 0;
-  return splitk_ticket_bytes(tiles) + static_cast<int64_t>(tiles) * splits * BM * 64 * 4;
+  return kSyncBytes + splitk_ticket_bytes(tiles) + static_cast<int64_t>(tiles) * splits * BM * 64 * 4;
 }
+
+// In-kernel activation quantise of wbk_linear_fp8_f16 (default on;
+// WBK_LINEAR_FUSED=0 runs the quantiser kernel and then the GEMM instead).
+bool linear_fused_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_LINEAR_FUSED");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// The fp16 activation side of wbk_linear_fp8_f16 when the GEMM quantises A itself.
+struct QuantIn {
+  const void* a16;
+  int a_fmt;
+  void* a_q;
+  float* scale_out;
+  uint32_t* amax_out;
+};
+
+int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int a_fmt, int w_fmt, float alpha,
+              const float* a_scale, const float* w_scale, const void* bias, const void* residual, void* out,
+              int epilogue, uint32_t* out_amax_bits, void* workspace, int64_t workspace_bytes, cudaStream_t s,
+              const QuantIn* qin);
 
 }  // namespace
 }  // namespace wbk
@@ -926,9 +1133,12 @@ using namespace wbk;
 extern "C" {
 
 int64_t wbk_gemm_fp8_ws_bytes(int64_t M, int64_t N, int64_t K) {
+  if (M <= 0) return 0;
   int splits = 0, tiles = 0;
   splitk_plan(M, N, K, &splits, &tiles);
-  return splitk_ws_bytes(splits, tiles);
+  int64_t need = splitk_ws_bytes(splits, tiles);
+  if (M <= BM && need < kSyncBytes) need = kSyncBytes;  // wbk_linear_fp8_f16's quantise sync words
+  return need;
 }
 
 int wbk_gemm_fp8(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int a_fmt, int w_fmt, float alpha,
@@ -942,6 +1152,46 @@ int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t 
                     const float* a_scale, const float* w_scale, const void* bias, const void* residual, void* out,
                     int epilogue, uint32_t* out_amax_bits, void* workspace, int64_t workspace_bytes,
                     wbk_stream_t stream) {
+  return gemm_impl(A, W, M, N, K, a_fmt, w_fmt, alpha, a_scale, w_scale, bias, residual, out, epilogue, out_amax_bits,
+                   workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream), nullptr);
+}
+
+int wbk_linear_fp8_f16(const void* A16, int64_t M, int64_t N, int64_t K, int a_fmt, void* a_q_out, float* a_scale_out,
+                       uint32_t* a_amax_ws, const void* W, int w_fmt, const float* w_scale, float alpha,
+                       const void* bias, const void* residual, void* out, int epilogue, uint32_t* out_amax_bits,
+                       void* workspace, int64_t workspace_bytes, wbk_stream_t stream) {
+  if (a_fmt != WBK_FMT_E4M3 && a_fmt != WBK_FMT_E5M2)
+    return fail(WBK_ERR_INVALID_ARG, "wbk_linear_fp8_f16: unknown fp8 format %d", a_fmt);
+  if (a_scale_out == nullptr || a_amax_ws == nullptr)
+    return fail(WBK_ERR_INVALID_ARG, "wbk_linear_fp8_f16: a_scale_out and a_amax_ws are required");
+  if (M < 0 || N <= 0 || K <= 0 || M > INT32_MAX || K > INT32_MAX)
+    return fail(WBK_ERR_INVALID_ARG, "wbk_linear_fp8_f16: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
+                (long long)K);
+  if (M > 0 && (A16 == nullptr || a_q_out == nullptr))
+    return fail(WBK_ERR_INVALID_ARG, "wbk_linear_fp8_f16: null activation pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool fused = linear_fused_enabled() && M > 0 && M <= BM && K % 16 == 0 && aligned(A16, 16) &&
+                     aligned(a_q_out, 16) && workspace != nullptr;
+  if (fused) {
+    const QuantIn q{A16, a_fmt, a_q_out, a_scale_out, a_amax_ws};
+    return gemm_impl(a_q_out, W, M, N, K, a_fmt, w_fmt, alpha, nullptr, w_scale, bias, residual, out, epilogue,
+                     out_amax_bits, workspace, workspace_bytes, s, &q);
+  }
+  // Two launches: the quantiser kernel, then the GEMM on its codes and scale.
+  if (int e = wbk_quantise_f16(A16, M * K, a_fmt, a_q_out, a_scale_out, a_amax_ws, stream)) return e;
+  return gemm_impl(a_q_out, W, M, N, K, a_fmt, w_fmt, alpha, a_scale_out, w_scale, bias, residual, out, epilogue,
+                   out_amax_bits, workspace, workspace_bytes, s, nullptr);
+}
+
+}  // extern "C"
+
+namespace wbk {
+namespace {
+
+int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int a_fmt, int w_fmt, float alpha,
+              const float* a_scale, const float* w_scale, const void* bias, const void* residual, void* out,
+              int epilogue, uint32_t* out_amax_bits, void* workspace, int64_t workspace_bytes, cudaStream_t s,
+              const QuantIn* qin) {
   if (M < 0 || N <= 0 || K <= 0)
     return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8: bad shape M=%lld N=%lld K=%lld", (long long)M, (long long)N,
                 (long long)K);
@@ -1002,7 +1252,7 @@ int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t 
     maps.w3 = tw;
   }
 
-  Params p;
+  QuantParams p;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -1017,19 +1267,43 @@ int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t 
   p.splits = 1;
   p.ws_partials = nullptr;
   p.ws_tickets = nullptr;
+  if (workspace != nullptr && !aligned(workspace, 256))
+    return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8_ws: workspace must be 256-byte aligned");
+  if (qin != nullptr && workspace_bytes < kSyncBytes)
+    return fail(WBK_ERR_INVALID_ARG, "wbk_linear_fp8_f16: workspace of %lld bytes, needs %lld",
+                (long long)workspace_bytes, (long long)kSyncBytes);
   if (workspace != nullptr && !pair && bn == 64) {
     int splits = 1, tiles = 0;
     splitk_plan(M, N, K, &splits, &tiles);
     const int64_t need = splitk_ws_bytes(splits, tiles);
     if (splits > 1) {
-      if (!aligned(workspace, 256)) return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8_ws: workspace must be 256-byte aligned");
       if (workspace_bytes < need)
         return fail(WBK_ERR_INVALID_ARG, "wbk_gemm_fp8_ws: workspace of %lld bytes, needs %lld",
                     (long long)workspace_bytes, (long long)need);
       p.splits = splits;
-      p.ws_tickets = static_cast<uint32_t*>(workspace);
-      p.ws_partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + splitk_ticket_bytes(tiles));
+      p.ws_tickets = reinterpret_cast<uint32_t*>(static_cast<char*>(workspace) + kSyncBytes);
+      p.ws_partials =
+          reinterpret_cast<float*>(static_cast<char*>(workspace) + kSyncBytes + splitk_ticket_bytes(tiles));
     }
+  }
+  p.a_f16 = nullptr;
+  p.a_q = nullptr;
+  p.a_scale_out = nullptr;
+  p.a_amax_out = nullptr;
+  p.qsync = nullptr;
+  p.a_vecs = 0;
+  p.a_max_fp8 = 0.0f;
+  p.a_e5m2 = 0;
+  if (qin != nullptr) {
+    if (bn != 64 || pair) return fail(WBK_ERR_UNSUPPORTED, "wbk_linear_fp8_f16: in-kernel quantise needs M <= 128");
+    p.a_f16 = static_cast<const __half*>(qin->a16);
+    p.a_q = static_cast<uint8_t*>(qin->a_q);
+    p.a_scale_out = qin->scale_out;
+    p.a_amax_out = qin->amax_out;
+    p.qsync = static_cast<uint32_t*>(workspace);
+    p.a_vecs = M * K / 8;
+    p.a_max_fp8 = fmt_max(qin->a_fmt);
+    p.a_e5m2 = qin->a_fmt == WBK_FMT_E5M2 ? 1 : 0;
   }
   p.num_items = p.num_tiles * p.splits;
   p.alpha = alpha;
@@ -1048,17 +1322,22 @@ int wbk_gemm_fp8_ws(const void* A, const void* W, int64_t M, int64_t N, int64_t 
             (static_cast<uint32_t>(bn >> 3) << 17) | (static_cast<uint32_t>(tile_rows >> 4) << 24);
   p.timeout_ns = wait_timeout_ns();
 
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (pair) {
     const int pairs = sms / 2;
     const int grid = 2 * static_cast<int>(num_tiles < pairs ? num_tiles : pairs);
     return dispatch_epi<256, true>(epilogue, vec, maps, p, grid, s);
   }
   const int grid = p.num_items < sms ? p.num_items : sms;
+  if (qin != nullptr) return dispatch_epi<64, false, true>(epilogue, vec, maps, p, grid, s);
   if (bn == 64) return dispatch_epi<64>(epilogue, vec, maps, p, grid, s);
   if (bn == 128) return dispatch_epi<128>(epilogue, vec, maps, p, grid, s);
   return dispatch_epi<256>(epilogue, vec, maps, p, grid, s);
 }
+
+}  // namespace
+}  // namespace wbk
+
+extern "C" {
 
 int wbk_device_error(uint32_t* code_out) {
   if (code_out == nullptr) return fail(WBK_ERR_INVALID_ARG, "wbk_device_error: null pointer");

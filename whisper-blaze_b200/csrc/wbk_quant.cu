@@ -1,12 +1,14 @@
 // Per-tensor FP8 (E4M3 / E5M2) amax, quantise and dequantise kernels for B200.
 //
-// This translation unit is compiled with --use_fast_math, the flag set the
-// reference builds its quantiser with (setup.py:41-54), so that the scale
-// expression `amax / max_fp8` (max_fp8 a runtime value) is evaluated by the
-// same compiler division as the reference's compute_scale_kernel
-// (csrc/kernels/fp8_quantize.cu:72). Everything else here is exact in either
-// mode: fp16->fp32 conversion, one fp32 multiply per element, fminf/fmaxf and
-// the hardware round-to-nearest-even, saturate-to-finite fp8 conversion.
+// The scale rule and the per-element conversion live in wbk_fp8_quant.cuh,
+// shared with the GEMM that quantises its own activations. The reference
+// builds its quantiser with fast math (setup.py:41-54), so its
+// compute_scale_kernel (csrc/kernels/fp8_quantize.cu:72) divides with the
+// approximate quotient; the shared rule names that quotient (__fdividef).
+// This unit keeps --use_fast_math for its other arithmetic, all of which is
+// exact in either mode: fp16->fp32 conversion, one fp32 multiply per element
+// (no fp32 denormals arise from fp16 inputs and these scales), fminf/fmaxf
+// and the hardware round-to-nearest-even, saturate-to-finite fp8 conversion.
 //
 // Layout in HBM: the input is a flat fp16 array (any shape, contiguous); the
 // output is a flat uint8 array of the same element count. Each thread moves
@@ -15,13 +17,13 @@
 #include <vector>
 
 #include "wbk_common.cuh"
+#include "wbk_fp8_quant.cuh"
 
 namespace wbk {
 namespace {
 
 constexpr int kThreads = 256;
 
-__host__ __device__ constexpr float fmt_max(int fmt) { return fmt == WBK_FMT_E4M3 ? 448.0f : 57344.0f; }
 
 // -------------------------------------------------------------------- amax
 
@@ -77,33 +79,6 @@ amax_f16_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ 
 }
 
 // ---------------------------------------------------------------- quantise
-
-// The reference's scale rule: scale = amax / max_fp8, replaced by 1.0 unless
-// it is > 0 (fp8_quantize.cu:72 and :218); inv_scale = 1/scale rounded to
-// nearest (host IEEE division at fp8_quantize.cu:224; __frcp_rn is the
-// correctly rounded reciprocal, so the two agree for every scale).
-__device__ __forceinline__ void scale_from_amax(uint32_t amax_bits, float max_fp8, float& scale, float& inv) {
-  const float amax = half_bits_to_float(amax_bits);
-  float s = amax / max_fp8;
-  s = (s > 0.0f) ? s : 1.0f;
-  scale = s;
-  inv = __frcp_rn(s);
-}
-
-template <int kFmt>
-__device__ __forceinline__ uint32_t q8x2(float a, float b, float inv, float mx) {
-  float2 f;
-  f.x = fminf(fmaxf(a * inv, -mx), mx);
-  f.y = fminf(fmaxf(b * inv, -mx), mx);
-  return __nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, kFmt == WBK_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2);
-}
-
-template <int kFmt>
-__device__ __forceinline__ uint32_t q8x4(uint32_t h01, uint32_t h23, float inv, float mx) {
-  const float2 f01 = __half22float2(*reinterpret_cast<const __half2*>(&h01));
-  const float2 f23 = __half22float2(*reinterpret_cast<const __half2*>(&h23));
-  return q8x2<kFmt>(f01.x, f01.y, inv, mx) | (q8x2<kFmt>(f23.x, f23.y, inv, mx) << 16);
-}
 
 template <int kFmt, bool kVec>
 __global__ void __launch_bounds__(kThreads)

@@ -55,6 +55,8 @@ _PROTOTYPES = {
     "wbk_gemm_fp8_ws": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _i32, _f32, _vp, _vp, _vp, _vp, _vp, _i32, _vp,
                                _vp, _i64, _vp]),
     "wbk_gemm_fp8_ws_bytes": (_i64, [_i64, _i64, _i64]),
+    "wbk_linear_fp8_f16": (_i32, [_vp, _i64, _i64, _i64, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _f32, _vp, _vp, _vp,
+                                  _i32, _vp, _vp, _i64, _vp]),
 }
 
 _lock = threading.Lock()

@@ -44,11 +44,13 @@ class BlazeLinear(nn.Module):
             return nn.functional.linear(x, self.weight, self.bias if self._has_bias else None)
         act = self.layer_prec.activation
         afmt = act.fmt() if act.is_fp8() else "e4m3"
-        a_fp8, a_scale = ops.quantise(x.half().contiguous(), afmt)
         wfmt = self.layer_prec.weight.fmt() if self.layer_prec.weight.is_fp8() else "e4m3"
         if self._w_fp8 is None:
             self._quantise_weights_as(wfmt)
-        return ops.gemm_fp8(a_fp8, a_scale, self._w_fp8, self._w_scale, self._bias16, a_format=afmt, w_format=wfmt)
+        # quantise(x) then the scaled GEMM; one kernel for short M (decoder steps)
+        out, _, _ = ops.linear_fp8(x.half().contiguous(), self._w_fp8, self._w_scale, self._bias16, a_format=afmt,
+                                   w_format=wfmt)
+        return out
 
     def _quantise_weights_as(self, fmt: str) -> None:
         w16 = self.weight.detach().to("cuda", torch.float16).contiguous()

@@ -282,6 +282,27 @@ def splitk_workspace(device, nbytes: int) -> Optional[torch.Tensor]:
     return ws
 
 
+def _check_epilogue_args(epilogue, M: int, N: int, out_shape, bias, residual, out_amax) -> int:
+    epi = _EPI_BY_NAME.get(epilogue)
+    if epi is None:
+        raise ValueError(f"unknown epilogue {epilogue!r}")
+    if bias is not None:
+        require_input(bias, "bias")
+        require_fp16(bias, "bias")
+        if bias.numel() != N:
+            raise RuntimeError(f"bias must have {N} elements")
+    if residual is not None:
+        require_input(residual, "residual")
+        require_fp16(residual, "residual")
+        if residual.numel() != M * N:
+            raise RuntimeError(f"residual must have shape {out_shape}")
+    if epi in (EPI_RESIDUAL, EPI_RESIDUAL_CLAMP) and residual is None:
+        raise RuntimeError("residual epilogue requires a residual tensor")
+    if epi == EPI_BIAS_MAXKEY and out_amax is None:
+        raise RuntimeError("the bias_maxkey epilogue requires out_amax")
+    return epi
+
+
 def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
              bias: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None, epilogue="none",
              a_format="e4m3", w_format="e4m3", out: Optional[torch.Tensor] = None,
@@ -307,24 +328,8 @@ def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
     if a.dim() < 1 or a.shape[-1] != K:
         raise RuntimeError(f"a_fp8 last dimension {a.shape[-1] if a.dim() else None} != K={K}")
     M = a.numel() // K if K else 0
-    epi = _EPI_BY_NAME.get(epilogue)
-    if epi is None:
-        raise ValueError(f"unknown epilogue {epilogue!r}")
     out_shape = tuple(a.shape[:-1]) + (N,)
-    if bias is not None:
-        require_input(bias, "bias")
-        require_fp16(bias, "bias")
-        if bias.numel() != N:
-            raise RuntimeError(f"bias must have {N} elements")
-    if residual is not None:
-        require_input(residual, "residual")
-        require_fp16(residual, "residual")
-        if residual.numel() != M * N:
-            raise RuntimeError(f"residual must have shape {out_shape}")
-    if epi in (EPI_RESIDUAL, EPI_RESIDUAL_CLAMP) and residual is None:
-        raise RuntimeError("residual epilogue requires a residual tensor")
-    if epi == EPI_BIAS_MAXKEY and out_amax is None:
-        raise RuntimeError("the bias_maxkey epilogue requires out_amax")
+    epi = _check_epilogue_args(epilogue, M, N, out_shape, bias, residual, out_amax)
     alpha_a, pa = _scale_arg(a_scale, "a_scale", a.device)
     alpha_w, pw = _scale_arg(w_scale, "w_scale", a.device)
     alpha = float(torch.tensor(alpha_a, dtype=torch.float32) * torch.tensor(alpha_w, dtype=torch.float32))
@@ -341,6 +346,52 @@ def gemm_fp8(a: torch.Tensor, a_scale: Scale, w: torch.Tensor, w_scale: Scale,
               "gemm_fp8")
     _count()
     return o
+
+
+def linear_fp8(x: torch.Tensor, w: torch.Tensor, w_scale: Scale, bias: Optional[torch.Tensor] = None,
+               residual: Optional[torch.Tensor] = None, epilogue="none", a_format="e4m3", w_format="e4m3",
+               out: Optional[torch.Tensor] = None, out_amax: Optional[torch.Tensor] = None,
+               q_out: Optional[torch.Tensor] = None, scale_out: Optional[torch.Tensor] = None,
+               amax_ws: Optional[torch.Tensor] = None,
+               workspace: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """FP8 linear on an fp16 activation: quantise(x) then gemm_fp8, as one call.
+
+    x: fp16 [..., K]; w: fp8 codes [N, K]. Returns (out fp16 [..., N], x's codes
+    uint8 [..., K], x's scale fp32 [1]) -- the codes and scale are exactly what
+    quantise(x) returns, the output exactly gemm_fp8 of them. For M <= 128 rows
+    this is one kernel (the GEMM quantises x itself) using `workspace` or the
+    device's shared one; otherwise the quantiser kernel and the GEMM.
+    """
+    require_input(x, "x")
+    require_fp16(x, "x")
+    require_input(w, "w_fp8")
+    require_bytes(w, "w_fp8")
+    if w.dim() != 2:
+        raise RuntimeError("w_fp8 must be 2-D [N, K]")
+    N, K = w.shape
+    if x.dim() < 1 or x.shape[-1] != K:
+        raise RuntimeError(f"x last dimension {x.shape[-1] if x.dim() else None} != K={K}")
+    M = x.numel() // K if K else 0
+    out_shape = tuple(x.shape[:-1]) + (N,)
+    epi = _check_epilogue_args(epilogue, M, N, out_shape, bias, residual, out_amax)
+    alpha, pw = _scale_arg(w_scale, "w_scale", x.device)
+    q = torch.empty(x.shape, dtype=torch.uint8, device=x.device) if q_out is None else q_out
+    sc = torch.empty(1, dtype=torch.float32, device=x.device) if scale_out is None else scale_out
+    aws = torch.empty(1, dtype=torch.int32, device=x.device) if amax_ws is None else amax_ws
+    o = torch.empty(out_shape, dtype=torch.float16, device=x.device) if out is None else out
+    require_same_device(x, w, bias, residual, o, out_amax, q, sc, aws, workspace)
+    with torch.cuda.device(x.device):
+        ws = None
+        if 0 < M <= 128:
+            need = lib().wbk_gemm_fp8_ws_bytes(M, N, K)
+            ws = workspace if workspace is not None else splitk_workspace(x.device, need)
+        check(lib().wbk_linear_fp8_f16(x.data_ptr(), M, N, K, fmt_code(a_format), q.data_ptr(), sc.data_ptr(),
+                                       aws.data_ptr(), w.data_ptr(), fmt_code(w_format), pw, alpha, ptr(bias),
+                                       ptr(residual), o.data_ptr(), epi, ptr(out_amax), ptr(ws),
+                                       0 if ws is None else ws.numel(), stream_of(x)),
+              "linear_fp8")
+    _count(1 if 0 < M <= 128 else 2)
+    return o, q, sc
 
 
 # ---------------------------------------------------------------- attention
