@@ -78,6 +78,32 @@ def test_gemm_vocab_projection(cuda_device):
     _check(y, _ref(aq, sa, wq, sw, None))
 
 
+# The skinny kernel (A resident in shared memory, weight-only ring) serves M <= 64 with at most
+# 12 K blocks (K <= 1536) in the one-call linear, and plain GEMMs with more tiles than SMs. Its
+# edges, with every epilogue, plus the first K past it: the linear's codes, scale and output
+# equal the standalone quantiser and gemm_fp8 on those codes, which meet the oracle gate.
+@pytest.mark.parametrize("epi,name", [(gemm.EPI_NONE, "none"), (gemm.EPI_GELU, "gelu"),
+                                      (gemm.EPI_RESIDUAL, "residual"), (gemm.EPI_RESIDUAL_CLAMP, "residual_clamp")])
+@pytest.mark.parametrize("M,N,K", [(64, 51866, 1280),   # vocab: 811 tiles on 148 CTAs, ragged unaligned N
+                                   (33, 4000, 1536),    # 12 K blocks: the largest resident A
+                                   (64, 1000, 1424),    # K % 128 != 0: per-block 2-D loads, zero-filled tail
+                                   (2, 72, 16),         # one partial K block
+                                   (64, 520, 1552)])    # 13 K blocks: the general kernel
+def test_gemm_skinny_edges(cuda_device, epi, name, M, N, K):
+    x = randn_f16((M, K), 71 + K).to(cuda_device)
+    wq, sw = ops.quantise(randn_f16((N, K), 72 + K, std=0.02).to(cuda_device))
+    b = randn_f16((N,), 73, std=0.02).to(cuda_device)
+    res = randn_f16((M, N), 74).to(cuda_device) if epi in (gemm.EPI_RESIDUAL, gemm.EPI_RESIDUAL_CLAMP) else None
+    aq, sa = ops.quantise(x)
+    out = torch.full((M, N), float("nan"), dtype=torch.float16, device=cuda_device)
+    y = ops.gemm_fp8(aq, sa, wq, sw, b, res, name, out=out)
+    _check(y, _ref(aq, sa, wq, sw, b, res, epi))
+    assert torch.equal(y, ops.gemm_fp8(aq, sa, wq, sw, b, res, name))  # deterministic
+    y_lin, q_lin, s_lin = ops.linear_fp8(x, wq, sw, b, res, name)
+    assert torch.equal(q_lin, aq) and torch.equal(s_lin, sa)
+    assert torch.equal(y_lin.view(torch.int16), y.view(torch.int16))
+
+
 @pytest.mark.parametrize("epi,name", [(gemm.EPI_GELU, "gelu"), (gemm.EPI_RESIDUAL, "residual"),
                                       (gemm.EPI_RESIDUAL_CLAMP, "residual_clamp")])
 @pytest.mark.parametrize("M,N,K", [(384, 5120, 1280), (200, 1280, 1280), (77, 40, 64), (4096, 2560, 640)])
@@ -210,3 +236,48 @@ def test_gemm_split_k_shared_workspace_across_shapes(cuda_device):
         for aq, sa, wq, sw, b, ref in ops_:
             y = ops.gemm_fp8(aq, sa, wq, sw, b)
             assert gemm.rel_error(y.float().cpu(), ref.float().cpu()) <= 1e-2
+
+
+_GENERAL_KERNEL_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, {tests!r})
+from conftest import randn_f16
+from whisper_blaze_b200 import ops
+dev = torch.device("cuda:0")
+outs = []
+for (M, N, K, epi) in {cases!r}:
+    x = randn_f16((M, K), M + K).to(dev)
+    w = randn_f16((N, K), N, std=0.02).to(dev)
+    b = randn_f16((N,), 5, std=0.02).to(dev)
+    res = randn_f16((M, N), 6).to(dev) if epi.startswith("residual") else None
+    wq, sw = ops.quantise(w)
+    y, q, s = ops.linear_fp8(x, wq, sw, b, res, epi)
+    y2 = ops.gemm_fp8(q, s, wq, sw, b, res, epi)
+    outs.append((y.cpu(), q.cpu(), s.cpu(), y2.cpu()))
+torch.save(outs, {path!r})
+"""
+
+
+def test_skinny_kernel_matches_general_kernel(cuda_device, tmp_path):
+    """The skinny kernel (and its in-kernel quantise) gives bit-identical codes, scales and
+    outputs to the general 64-wide kernel (WBK_GEMM_SKINNY=0, run in a subprocess)."""
+    import os
+    import subprocess
+    import sys
+    cases = [(64, 1280, 1280, "none"), (64, 3840, 1280, "residual"), (17, 640, 1296, "gelu"), (5, 51866, 1280, "none")]
+    path = str(tmp_path / "general.pt")
+    script = _GENERAL_KERNEL_SCRIPT.format(tests=os.path.dirname(os.path.abspath(__file__)), cases=cases, path=path)
+    env = dict(os.environ, WBK_GEMM_SKINNY="0")
+    subprocess.run([sys.executable, "-c", script], env=env, check=True, timeout=600)
+    general = torch.load(path)
+    for (M, N, K, epi), (yg, qg, sg, y2g) in zip(cases, general):
+        x = randn_f16((M, K), M + K).to(cuda_device)
+        w = randn_f16((N, K), N, std=0.02).to(cuda_device)
+        b = randn_f16((N,), 5, std=0.02).to(cuda_device)
+        res = randn_f16((M, N), 6).to(cuda_device) if epi.startswith("residual") else None
+        wq, sw = ops.quantise(w)
+        y, q, s = ops.linear_fp8(x, wq, sw, b, res, epi)
+        y2 = ops.gemm_fp8(q, s, wq, sw, b, res, epi)
+        assert torch.equal(q.cpu(), qg) and torch.equal(s.cpu(), sg), (M, N, K)
+        assert torch.equal(y.cpu().view(torch.int16), yg.view(torch.int16)), (M, N, K, "linear")
+        assert torch.equal(y2.cpu().view(torch.int16), y2g.view(torch.int16)), (M, N, K, "gemm")

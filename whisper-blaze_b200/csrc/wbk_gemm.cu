@@ -93,6 +93,14 @@ enum : uint32_t {
   SITE_SELFTEST = 15,
 };
 
+// Shared-memory scratch of the in-kernel activation quantise.
+struct QuantScratch {
+  uint32_t red[THREADS / 32];  // per-warp amax
+  uint32_t amax;
+  float scale, inv;
+  int ok;
+};
+
 template <int kBN, bool kPair = false>
 struct SharedStorage {
   uint8_t a[Tile<kBN, kPair>::STAGES][Tile<kBN, kPair>::A_STAGE_BYTES];  // 1024-byte aligned (swizzle atom)
@@ -105,11 +113,7 @@ struct SharedStorage {
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
-  // in-kernel activation quantise (short-M linear): per-warp amax, the scale, status
-  uint32_t qred[THREADS / 32];
-  uint32_t qamax;
-  float qscale, qinv;
-  int qok;
+  QuantScratch q;  // in-kernel activation quantise (short-M linear)
 };
 template <int kBN, bool kPair = false>
 constexpr size_t smem_bytes() { return sizeof(SharedStorage<kBN, kPair>) + 1024; }
@@ -196,6 +200,77 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
 
 // Generic-proxy global writes <-> async-proxy (TMA) reads of the same bytes.
 __device__ __forceinline__ void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// In-kernel per-tensor quantise of A (cooperative launch, all THREADS threads
+// of every CTA): each CTA takes the amax of its slice of a_f16, the grid agrees
+// on the tensor's amax through one bounded grid-wide arrival, each CTA writes
+// its slice's codes to a_q (read back by TMA afterwards), and after a second
+// arrival CTA 0 publishes the scale and amax bits. The last CTA through zeroes
+// the sync words for the next call. Returns false (timeout recorded) if an
+// arrival gave up; the result is the same in every thread of the CTA.
+// The arrivals are led by thread kQuantLeader, not thread 0: once A's loads for
+// the amax have landed (so they do not queue behind the weight stream), thread
+// 0 runs `issue_weights` (the early weight loads) while the leader arrives.
+constexpr int kQuantLeader = 96;
+template <class IssueWeights>
+__device__ __forceinline__ bool quantise_a_prologue(const QuantParams& p, QuantScratch& q, IssueWeights&& issue_weights) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t v0 = p.a_vecs * blockIdx.x / gridDim.x;
+  const int64_t v1 = p.a_vecs * (blockIdx.x + 1) / gridDim.x;
+  const uint4* src = reinterpret_cast<const uint4*>(p.a_f16);
+  uint32_t m = 0;
+  for (int64_t i = v0 + threadIdx.x; i < v1; i += THREADS) m = max(m, absmax8_bits(__ldcg(src + i)));
+  m = warp_max_u32(m);
+  if (lane == 0) q.red[warp] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) issue_weights();
+  if (threadIdx.x == kQuantLeader) {
+    uint32_t mm = 0;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; ++w) mm = max(mm, q.red[w]);
+    if (mm != 0u) atomicMax(p.qsync + 3, mm);
+    const bool ok = grid_arrive_wait(p.qsync + 0, gridDim.x, p.timeout_ns);
+    const uint32_t amax = ok ? ld_acquire_gpu(p.qsync + 3) : 0u;
+    float sc, inv;
+    scale_from_amax(amax, p.a_max_fp8, sc, inv);
+    q.amax = amax;
+    q.scale = sc;
+    q.inv = inv;
+    q.ok = ok ? 1 : 0;
+  }
+  __syncthreads();
+  if (q.ok) {
+    const float inv = q.inv, mx = p.a_max_fp8;
+    uint2* dst = reinterpret_cast<uint2*>(p.a_q);
+    for (int64_t i = v0 + threadIdx.x; i < v1; i += THREADS) {
+      const uint4 v = __ldcg(src + i);
+      dst[i] = p.a_e5m2 ? make_uint2(q8x4<WBK_FMT_E5M2>(v.x, v.y, inv, mx), q8x4<WBK_FMT_E5M2>(v.z, v.w, inv, mx))
+                        : make_uint2(q8x4<WBK_FMT_E4M3>(v.x, v.y, inv, mx), q8x4<WBK_FMT_E4M3>(v.z, v.w, inv, mx));
+    }
+    fence_async_global();  // the codes are read back by TMA (async proxy), in other CTAs too
+    __threadfence();
+  }
+  __syncthreads();
+  if (threadIdx.x == kQuantLeader && q.ok) {
+    const bool ok = grid_arrive_wait(p.qsync + 1, gridDim.x, p.timeout_ns);
+    if (ok) {
+      if (blockIdx.x == 0) {
+        if (p.a_scale_out != nullptr) *p.a_scale_out = q.scale;
+        if (p.a_amax_out != nullptr) *p.a_amax_out = q.amax;
+      }
+      // Every CTA has passed both arrivals once the last one leaves: nothing reads the words again.
+      if (atomicAdd(p.qsync + 2, 1u) == gridDim.x - 1u) {
+        p.qsync[0] = 0u;
+        p.qsync[1] = 0u;
+        p.qsync[3] = 0u;
+        p.qsync[2] = 0u;
+      }
+    }
+    q.ok = ok ? 1 : 0;
+  }
+  __syncthreads();
+  return q.ok != 0;
+}
 
 // ----------------------------------------------------------------- epilogue
 
@@ -399,18 +474,19 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     }
   };
 
-  // In-kernel quantise of A (short-M linear). The W boxes of the first stages
-  // go out first and stream in meanwhile. Then every CTA takes the amax of its
-  // slice of A, the grid agrees on the tensor's amax (one bounded grid-wide
-  // arrival; the launch is cooperative, so all CTAs are resident), each CTA
-  // writes its slice's codes, and after a second arrival the pipeline below
-  // TMA-loads A from those codes as usual. The last CTA through zeroes the
-  // sync words for the next call.
+  // In-kernel quantise of A (short-M linear). Every CTA takes the amax of its
+  // slice of A; the W boxes of the first stages go out once those loads have
+  // landed and stream in meanwhile. The grid agrees on the tensor's amax (one
+  // bounded grid-wide arrival; the launch is cooperative, so all CTAs are
+  // resident), each CTA writes its slice's codes, and after a second arrival
+  // the pipeline below TMA-loads A from those codes as usual. The last CTA
+  // through zeroes the sync words for the next call.
   int pre = 0;  // stages whose W half was issued ahead of the quantise
   bool run = true;
   if constexpr (kQuantA) {
     static_assert(!kPair, "the in-kernel quantise is for single-CTA tiles");
-    if (warp == 0 && lane == 0 && first_tile < p.num_items) {
+    run = quantise_a_prologue(p, s.q, [&]() {
+      if (first_tile >= p.num_items) return;
       const int tile = first_tile / p.splits;
       int kb0, kb1;
       split_range(p, TL::G, first_tile - tile * p.splits, kb0, kb1);
@@ -419,61 +495,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         mbar_arrive_expect_tx(&s.full[pre], TL::G * (p.a_box_bytes + TL::B_SUB_BYTES));
         load_stage(pre, kb, 0, n0, false, true);
       }
-    }
-    const int64_t v0 = p.a_vecs * blockIdx.x / gridDim.x;
-    const int64_t v1 = p.a_vecs * (blockIdx.x + 1) / gridDim.x;
-    const uint4* src = reinterpret_cast<const uint4*>(p.a_f16);
-    uint32_t m = 0;
-    for (int64_t i = v0 + threadIdx.x; i < v1; i += THREADS) m = max(m, absmax8_bits(__ldcg(src + i)));
-    m = warp_max_u32(m);
-    if (lane == 0) s.qred[warp] = m;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      uint32_t mm = 0;
-#pragma unroll
-      for (int w = 0; w < THREADS / 32; ++w) mm = max(mm, s.qred[w]);
-      if (mm != 0u) atomicMax(p.qsync + 3, mm);
-      const bool ok = grid_arrive_wait(p.qsync + 0, gridDim.x, p.timeout_ns);
-      const uint32_t amax = ok ? ld_acquire_gpu(p.qsync + 3) : 0u;
-      float sc, inv;
-      scale_from_amax(amax, p.a_max_fp8, sc, inv);
-      s.qamax = amax;
-      s.qscale = sc;
-      s.qinv = inv;
-      s.qok = ok ? 1 : 0;
-    }
-    __syncthreads();
-    if (s.qok) {
-      const float inv = s.qinv, mx = p.a_max_fp8;
-      uint2* dst = reinterpret_cast<uint2*>(p.a_q);
-      for (int64_t i = v0 + threadIdx.x; i < v1; i += THREADS) {
-        const uint4 v = __ldcg(src + i);
-        dst[i] = p.a_e5m2 ? make_uint2(q8x4<WBK_FMT_E5M2>(v.x, v.y, inv, mx), q8x4<WBK_FMT_E5M2>(v.z, v.w, inv, mx))
-                          : make_uint2(q8x4<WBK_FMT_E4M3>(v.x, v.y, inv, mx), q8x4<WBK_FMT_E4M3>(v.z, v.w, inv, mx));
-      }
-      fence_async_global();  // the codes are read back by TMA (async proxy), in other CTAs too
-      __threadfence();
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && s.qok) {
-      const bool ok = grid_arrive_wait(p.qsync + 1, gridDim.x, p.timeout_ns);
-      if (ok) {
-        if (blockIdx.x == 0) {
-          if (p.a_scale_out != nullptr) *p.a_scale_out = s.qscale;
-          if (p.a_amax_out != nullptr) *p.a_amax_out = s.qamax;
-        }
-        // Every CTA has passed both arrivals once the last one leaves: nothing reads the words again.
-        if (atomicAdd(p.qsync + 2, 1u) == gridDim.x - 1u) {
-          p.qsync[0] = 0u;
-          p.qsync[1] = 0u;
-          p.qsync[3] = 0u;
-          p.qsync[2] = 0u;
-        }
-      }
-      s.qok = ok ? 1 : 0;
-    }
-    __syncthreads();
-    run = s.qok != 0;
+    });
   }
 
   if constexpr (kQuantA) {
@@ -637,7 +659,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     const int ew = warp - 2;             // 0..7
     const int quarter = warp & 3;        // TMEM lanes this warp may access: 32*quarter ..
     const int col_half = ew >> 2;        // which 128 of the 256 accumulator columns
-    const float a_sc = kQuantA ? s.qscale : (p.a_scale ? __ldg(p.a_scale) : 1.0f);
+    const float a_sc = kQuantA ? s.q.scale : (p.a_scale ? __ldg(p.a_scale) : 1.0f);
     const float descale = p.alpha * a_sc * (p.w_scale ? __ldg(p.w_scale) : 1.0f);
     constexpr bool kSignedMax = (kEpi == WBK_EPI_BIAS_MAXKEY);
     float amax = kSignedMax ? -INFINITY : 0.0f;  // max |out|, or max out for the key epilogue
@@ -840,6 +862,372 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
   }
 }
 
+// ------------------------------------------------------ skinny (M <= 64) GEMM
+//
+// Decoder-step shapes (M <= 64 rows, K <= 1536) stream a large weight through
+// every SM for a small A. This kernel keeps A resident in shared memory, loaded
+// once per CTA (two K blocks per box and barrier), and gives the rest of shared
+// memory to a weight-only ring, so more of the weight stream is in flight and
+// no CTA re-reads A per tile. Tiles are 64 (or 128) output columns x all rows;
+// the MMA is M = 128, so TMEM lanes 64..127 hold rows that do not exist: A's K
+// blocks sit 8 KB (64 rows) apart and the MMA's rows 64..127 of block j read
+// block j+1 (or, for the last block, 8 KB of slack), and those rows are never
+// stored. Only the epilogue warps of lane quarters 0 and 1 (rows 0..63) work.
+// Same per-tile MMA sequence as fp8_gemm_kernel, so the outputs are identical.
+constexpr int kSkMaxStages = 12;
+constexpr int kSkRows = 64;                          // A rows held (M <= 64)
+constexpr int kSkABlock = kSkRows * BK;              // 8 KB per K block
+constexpr int kSkASlack = (BM - kSkRows) * BK;       // the MMA's last-block overrun
+constexpr int kSkEpiWarps = 4;                       // warps of lane quarters 0, 1 x two column halves
+constexpr int kSkMaxKBlocks = 12;                    // K <= 1536
+constexpr int kSkStageOut = 2 * STAGE_OUT_BYTES;     // per active epilogue warp, double-buffered
+
+template <int kBN>
+struct Skinny {
+  static constexpr int G = 2;                        // K blocks per weight stage
+  static constexpr int B_STAGE = G * kBN * BK;       // 16 KB (64-wide) / 32 KB (128-wide)
+  static constexpr int EPI_COLS = kBN / 2;           // columns per epilogue warp
+  static constexpr int TMEM_COLS = NUM_ACC * kBN;
+  static_assert(G == 2, "A's barriers cover two K blocks each, one weight stage");
+};
+
+struct SkinnyHeader {  // at the (1024-aligned) start of shared memory
+  uint64_t full[kSkMaxStages];
+  uint64_t empty[kSkMaxStages];
+  uint64_t a_full[kSkMaxKBlocks / 2];  // one per pair of A's K blocks
+  uint64_t acc_full[NUM_ACC];
+  uint64_t acc_empty[NUM_ACC];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  QuantScratch q;
+};
+constexpr int kSkHeaderBytes = 1024;
+static_assert(sizeof(SkinnyHeader) <= kSkHeaderBytes, "skinny header");
+
+struct SkinnyParams : QuantParams {
+  int stages;           // weight ring depth
+  uint32_t a_region;    // bytes of the resident A region (K blocks x 8 KB + slack), 1024-multiple
+  int a_grouped;        // 1: one 3-D box brings all of A
+};
+
+// Dynamic shared memory of a skinny launch.
+__host__ __device__ constexpr size_t skinny_smem(uint32_t a_region, int stages, int b_stage) {
+  return 1024 + kSkHeaderBytes + a_region + static_cast<size_t>(stages) * b_stage + kSkEpiWarps * kSkStageOut;
+}
+
+template <int kBN, int kEpi, bool kTmaStore, bool kQuantA>
+__global__ void __launch_bounds__(THREADS, 1)
+fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
+                  const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_a3,
+                  const __grid_constant__ CUtensorMap tmap_w3, const SkinnyParams p) {
+  using SK = Skinny<kBN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  SkinnyHeader& h = *reinterpret_cast<SkinnyHeader*>(base);
+  uint8_t* a_smem = base + kSkHeaderBytes;
+  uint8_t* b_smem = a_smem + p.a_region;
+  uint8_t* out_smem = b_smem + static_cast<size_t>(p.stages) * SK::B_STAGE;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int* abort_flag = &h.abort_flag;
+  const int stages = p.stages;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&h.full[i], 1);
+      mbar_init(&h.empty[i], 1);
+    }
+    for (int i = 0; i < kSkMaxKBlocks / 2; ++i) mbar_init(&h.a_full[i], 1);
+    for (int i = 0; i < NUM_ACC; ++i) {
+      mbar_init(&h.acc_full[i], 1);
+      mbar_init(&h.acc_empty[i], kSkEpiWarps);
+    }
+    mbar_init(&h.drain, 1);
+    h.abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (p.a_grouped) prefetch_tmap(&tmap_a3);
+    else prefetch_tmap(&tmap_a);
+    if (p.grouped) prefetch_tmap(&tmap_w3);
+    else prefetch_tmap(&tmap_w);
+    if (kTmaStore) prefetch_tmap(&tmap_out);
+  }
+  if (warp == 1) {
+    tmem_alloc(&h.tmem_base, SK::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = h.tmem_base;
+  griddep_wait();
+
+  // W boxes of K blocks [kb, kb + G) of the tile at column n0 into ring stage `st`.
+  auto load_w = [&](int st, int kb, int n0) {
+    uint8_t* dst = b_smem + static_cast<size_t>(st) * SK::B_STAGE;
+    if (p.grouped) {
+      tma_load_3d(&tmap_w3, &h.full[st], dst, 0, n0, kb);
+    } else {
+#pragma unroll
+      for (int g = 0; g < SK::G; ++g) tma_load_2d(&tmap_w, &h.full[st], dst + g * kBN * BK, (kb + g) * BK, n0);
+    }
+  };
+  // All of A (every K block, 64-row boxes) into the resident region, two K blocks
+  // per box and barrier, so the first MMAs wait for their own blocks only.
+  auto load_a = [&]() {
+    for (int j = 0; j * 2 < p.kblocks; ++j) {
+      const int nb = min(2, p.kblocks - 2 * j);
+      mbar_arrive_expect_tx(&h.a_full[j], static_cast<uint32_t>(p.a_grouped ? 2 : nb) * kSkABlock);
+      if (p.a_grouped) {
+        tma_load_3d(&tmap_a3, &h.a_full[j], a_smem + 2 * j * kSkABlock, 0, 0, 2 * j);
+      } else {
+        for (int kb = 2 * j; kb < 2 * j + nb; ++kb)
+          tma_load_2d(&tmap_a, &h.a_full[j], a_smem + kb * kSkABlock, kb * BK, 0);
+      }
+    }
+  };
+
+  int pre = 0;  // ring stages whose weight boxes went out before the in-kernel quantise
+  bool run = true;
+  if constexpr (kQuantA) {
+    run = quantise_a_prologue(p, h.q, [&]() {
+      for (int t = blockIdx.x, kb = 0; t < p.num_tiles && pre < stages; ++pre) {
+        mbar_arrive_expect_tx(&h.full[pre], SK::B_STAGE);
+        load_w(pre, kb, t * kBN);
+        kb += SK::G;
+        if (kb >= p.kblocks) {
+          kb = 0;
+          t += gridDim.x;
+        }
+      }
+    });
+    if (!run && warp == 0 && lane == 0) {
+      // complete the ring stages in flight before leaving (A's bytes are not used)
+      for (int i = 0; i < pre; ++i) {
+        int dummy = 0;
+        mbar_wait(&h.full[i], 0, &dummy, 1000000ull, SITE_DRAIN);
+      }
+    }
+  }
+
+  if (!run) {
+    // straight to the teardown
+  } else if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      if constexpr (kQuantA) fence_async_global();  // A's codes were written by the generic proxy
+      load_a();
+      int st = 0;
+      uint32_t phase = 0;
+      int n_st = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int n0 = tile * kBN;
+        for (int kb = 0; kb < p.kblocks; kb += SK::G) {
+          if (!(kQuantA && n_st < pre)) {
+            if (!mbar_wait(&h.empty[st], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&h.full[st], SK::B_STAGE);
+            load_w(st, kb, n0);
+          }
+          ++n_st;
+          if (++st == stages) {
+            st = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      int dummy = 0;
+      if (ok) {
+        for (int i = 0; i < stages; ++i) {  // every stage released: no commit arrival still in flight
+          if (!mbar_wait(&h.empty[st], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) break;
+          if (++st == stages) {
+            st = 0;
+            phase ^= 1u;
+          }
+        }
+      } else {
+        for (int i = 0; i < stages; ++i) {  // let the copies already issued land
+          const uint32_t ph = (i < st) ? phase : (phase ^ 1u);
+          mbar_wait(&h.full[i], ph, &dummy, 1000000ull, SITE_DRAIN);
+        }
+      }
+      for (int j = 0; j * 2 < p.kblocks; ++j) mbar_wait(&h.a_full[j], 0, &dummy, ok ? p.timeout_ns : 1000000ull, SITE_DRAIN);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int st = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      bool a_ready = false;  // every A block landed (checked during the first tile)
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&h.acc_empty[acc], acc_phase ^ 1u, abort_flag, p.timeout_ns, SITE_MMA_ACC_EMPTY)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
+        for (int kbs = 0; kbs < p.kblocks; kbs += SK::G) {
+          if (!mbar_wait(&h.full[st], phase, abort_flag, p.timeout_ns, SITE_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          if (!a_ready) {
+            if (!mbar_wait(&h.a_full[kbs >> 1], 0, abort_flag, p.timeout_ns, SITE_MMA_FULL)) {
+              ok = false;
+              break;
+            }
+            a_ready = kbs + SK::G >= p.kblocks;
+          }
+          tc_fence_after();
+          const uint8_t* bst = b_smem + static_cast<size_t>(st) * SK::B_STAGE;
+#pragma unroll
+          for (int g = 0; g < SK::G; ++g) {
+            const int kb = kbs + g;
+            if (kb >= p.kblocks) break;
+            const uint64_t adesc = make_sw128_desc(a_smem + kb * kSkABlock);
+            const uint64_t bdesc = make_sw128_desc(bst + g * kBN * BK);
+#pragma unroll
+            for (int k = 0; k < BK / UMMA_K; ++k) {
+              const uint64_t koff = static_cast<uint64_t>((k * UMMA_K) >> 4);
+              umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+            }
+          }
+          umma_commit(&h.empty[st]);
+          if (++st == stages) {
+            st = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&h.acc_full[acc]);
+        if (++acc == NUM_ACC) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      if (!ok) {
+        umma_commit(&h.drain);
+        int dummy = 0;
+        mbar_wait(&h.drain, 0, &dummy, 1000000ull, SITE_DRAIN);
+      }
+    }
+  } else if ((warp & 3) < 2) {
+    // --------------------------------------------------------- epilogue
+    const int quarter = warp & 3;                   // 0 or 1: rows 32*quarter ..
+    const int col_half = (warp - 2) >> 2;           // warps 4, 5: columns 0..; warps 8, 9: the second half
+    const int ew = col_half * 2 + quarter;          // 0..3
+    const float a_sc = kQuantA ? h.q.scale : (p.a_scale ? __ldg(p.a_scale) : 1.0f);
+    const float descale = p.alpha * a_sc * (p.w_scale ? __ldg(p.w_scale) : 1.0f);
+    constexpr bool kSignedMax = (kEpi == WBK_EPI_BIAS_MAXKEY);
+    float amax = kSignedMax ? -INFINITY : 0.0f;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    int sbuf = 0;
+    const int row0 = quarter * 32;
+    const int row = row0 + lane;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      const int n0 = tile * kBN + col_half * SK::EPI_COLS;
+      uint4 resa[4], resb[4];
+      prefetch_residual<kEpi, kTmaStore>(p, row, n0, resa);
+      if (!mbar_wait(&h.acc_full[acc], acc_phase, abort_flag, p.timeout_ns, SITE_EPI_ACC_FULL)) break;
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc * kBN + col_half * SK::EPI_COLS);
+      const int nchunks = min(SK::EPI_COLS / CHUNK, (p.N - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
+      auto process = [&](const uint32_t* regs, const uint4* res, int c) {
+        const int col0 = n0 + c * CHUNK;
+        float v[32];
+        epi_values<kEpi, kTmaStore>(p, regs, res, row, col0, descale, v);
+        const int valid_cols = (row < p.M) ? min(CHUNK, p.N - col0) : 0;
+        amax = kSignedMax ? max_valid(amax, v, valid_cols) : absmax_valid(amax, v, valid_cols);
+        uint32_t w[16];
+        pack_fp16(v, w);
+        if (kTmaStore) {
+          uint8_t* buf = out_smem + ew * kSkStageOut + sbuf * STAGE_OUT_BYTES;
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk16 = q ^ ((lane >> 1) & 3);
+            *reinterpret_cast<uint4*>(buf + lane * 64 + chunk16 * 16) =
+                make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_out, buf, col0, row0);
+            bulk_commit();
+          }
+          sbuf ^= 1;
+        } else if (row < p.M) {
+          __half* orow = p.out + static_cast<int64_t>(row) * p.N + col0;
+          if (p.out_pairs) {
+            uint32_t* o32 = reinterpret_cast<uint32_t*>(orow);
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+              if (2 * t + 1 < valid_cols) o32[t] = w[t];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < valid_cols)
+                orow[j] = __ushort_as_half(static_cast<unsigned short>((w[j >> 1] >> ((j & 1) * 16)) & 0xFFFFu));
+          }
+        }
+      };
+      uint32_t ra[32], rb[32];
+      if (nchunks > 0) {
+        tmem_ld_32x32b_x32(taddr, ra);
+        tmem_ld_wait(ra);
+      }
+#pragma unroll 1
+      for (int c = 0; c < nchunks; c += 2) {
+        const bool more1 = c + 1 < nchunks, more2 = c + 2 < nchunks;
+        if (more1) {
+          tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>((c + 1) * CHUNK), rb);
+          prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 1) * CHUNK, resb);
+        }
+        process(ra, resa, c);
+        if (more1) {
+          tmem_ld_wait(rb);
+          if (more2) {
+            tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>((c + 2) * CHUNK), ra);
+            prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 2) * CHUNK, resa);
+          }
+          process(rb, resb, c + 1);
+          if (more2) tmem_ld_wait(ra);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&h.acc_empty[acc]);
+      if (++acc == NUM_ACC) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+    if (kTmaStore && lane == 0) bulk_wait_read<0>();
+    if (p.out_amax != nullptr) {
+      const uint32_t hb = __half_as_ushort(__float2half_rn(amax));
+      const uint32_t bits = warp_max_u32(kSignedMax ? f16_order_key(hb) : hb);
+      if (lane == 0 && bits != 0u) atomicMax(p.out_amax, bits);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, SK::TMEM_COLS);
+  }
+}
+
+
 __global__ void selftest_wait_kernel(uint64_t timeout_ns) {
   __shared__ uint64_t bar;
   __shared__ int abort_flag;
@@ -974,6 +1362,68 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
 struct Maps {
   CUtensorMap a, w, out, a3, w3;
 };
+
+// Skinny kernel for M <= 64, K <= 1536 (default on; WBK_GEMM_SKINNY=0 uses the general kernel).
+bool skinny_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_GEMM_SKINNY");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <int kBN, int kEpi, bool kTma, bool kQuantA>
+int launch_skinny(const Maps& m, const SkinnyParams& p, int grid, cudaStream_t stream) {
+  static std::mutex mu;
+  static std::vector<char> configured;
+  const int dev = current_device();
+  if (dev < 0) return fail(WBK_ERR_CUDA, "no current CUDA device");
+  auto kernel = fp8_skinny_kernel<kBN, kEpi, kTma, kQuantA>;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
+    if (!configured[dev]) {
+      if (int e = cuda_check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 232448),
+                             "cudaFuncSetAttribute(max dynamic smem, skinny)"))
+        return e;
+      configured[dev] = 1;
+    }
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = skinny_smem(p.a_region, p.stages, Skinny<kBN>::B_STAGE);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  int nattr = 0;
+  if (kQuantA ? pdl_coop_enabled() : pdl_enabled()) {
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+  }
+  if (kQuantA) {  // the CTAs wait for one another: all must be resident at once
+    attr[nattr].id = cudaLaunchAttributeCooperative;
+    attr[nattr].val.cooperative = 1;
+    ++nattr;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = nattr;
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, m.a, m.w, m.out, m.a3, m.w3, p), "fp8 skinny gemm launch");
+}
+
+template <int kBN, bool kQuantA>
+int dispatch_skinny(int epilogue, bool tma, const Maps& m, const SkinnyParams& p, int grid, cudaStream_t s) {
+#define WBK_SK(E) \
+  return tma ? launch_skinny<kBN, E, true, kQuantA>(m, p, grid, s) : launch_skinny<kBN, E, false, kQuantA>(m, p, grid, s)
+  switch (epilogue) {
+    case WBK_EPI_NONE: WBK_SK(WBK_EPI_NONE);
+    case WBK_EPI_GELU: WBK_SK(WBK_EPI_GELU);
+    case WBK_EPI_RESIDUAL: WBK_SK(WBK_EPI_RESIDUAL);
+    case WBK_EPI_RESIDUAL_CLAMP: WBK_SK(WBK_EPI_RESIDUAL_CLAMP);
+    default: WBK_SK(WBK_EPI_BIAS_MAXKEY);
+  }
+#undef WBK_SK
+}
 
 template <int kBN, int kEpi, bool kPair, bool kQuantA>
 int dispatch_store(bool tma, const Maps& m, const QuantParams& p, int grid, cudaStream_t s) {
@@ -1237,15 +1687,42 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
   } else {
     to = ta;  // unused by the direct-store kernel
   }
-  // One 3-D load per operand per stage when K is a whole number of 128-byte blocks.
+  // Skinny path (A resident, weight-only ring): M <= 64, K <= 1536, no K split;
+  // used where it measured faster on B200: the in-kernel quantise (its early
+  // weight ring is deeper) and shapes with more tiles than SMs (A is not
+  // re-read per tile: 64 x 51866 x 1280 in 24.2 us against 26.4). With one
+  // tile per CTA its smaller weight stages cost ~0.4 us more than the general
+  // kernel's.
+  const int64_t kblocks_all = (K + BK - 1) / BK;
+  const int64_t tiles_if_skinny = (N + bn - 1) / bn;
+  bool skinny = skinny_enabled() && M <= kSkRows && !pair && (bn == 64 || bn == 128) &&
+                kblocks_all <= kSkMaxKBlocks && (qin != nullptr || tiles_if_skinny > sms);
+  if (skinny && workspace != nullptr) {
+    int sp = 1, st = 0;
+    splitk_plan(M, N, K, &sp, &st);
+    skinny = sp == 1;
+  }
+  const uint32_t sk_region = static_cast<uint32_t>(kblocks_all * kSkABlock + kSkASlack);
+  const int sk_bstage = bn == 64 ? Skinny<64>::B_STAGE : Skinny<128>::B_STAGE;
+  int sk_stages = 0;
+  if (skinny) {
+    const int64_t avail = 232448 - static_cast<int64_t>(skinny_smem(sk_region, 0, sk_bstage));
+    sk_stages = static_cast<int>(avail / sk_bstage);
+    if (sk_stages > kSkMaxStages) sk_stages = kSkMaxStages;
+    skinny = sk_stages >= 2;
+  }
+  // One 3-D load per operand per stage when K is a whole number of 128-byte blocks
+  // (the skinny kernel: two K blocks per box for A and for each W stage).
   const int group = bn == 64 ? Tile<64>::G : (pair ? Tile<256, true>::G : Tile<128>::G);
+  const int a_group = skinny ? 2 : group;  // the skinny kernel loads A two K blocks per box
+  const int w_group = skinny ? Skinny<64>::G : group;
   bool grouped = K % BK == 0 && kblocks_grouping_enabled();
   if (grouped) {
     // If the driver does not take the blocked view, fall back to per-block 2-D loads.
     grouped = make_tmap_kblocks(&maps.a3, A, static_cast<uint64_t>(K), static_cast<uint64_t>(M), a_box_rows,
-                                static_cast<uint32_t>(group)) == WBK_OK &&
+                                static_cast<uint32_t>(a_group)) == WBK_OK &&
               make_tmap_kblocks(&maps.w3, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N), w_box_rows,
-                                static_cast<uint32_t>(group)) == WBK_OK;
+                                static_cast<uint32_t>(w_group)) == WBK_OK;
   }
   if (!grouped) {
     maps.a3 = ta;  // unused: the kernel issues per-block 2-D loads
@@ -1295,7 +1772,8 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
   p.a_max_fp8 = 0.0f;
   p.a_e5m2 = 0;
   if (qin != nullptr) {
-    if (bn != 64 || pair) return fail(WBK_ERR_UNSUPPORTED, "wbk_linear_fp8_f16: in-kernel quantise needs M <= 128");
+    if (!skinny && (bn != 64 || pair))
+      return fail(WBK_ERR_UNSUPPORTED, "wbk_linear_fp8_f16: in-kernel quantise needs M <= 128");
     p.a_f16 = static_cast<const __half*>(qin->a16);
     p.a_q = static_cast<uint8_t*>(qin->a_q);
     p.a_scale_out = qin->scale_out;
@@ -1328,6 +1806,17 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
     return dispatch_epi<256, true>(epilogue, vec, maps, p, grid, s);
   }
   const int grid = p.num_items < sms ? p.num_items : sms;
+  if (skinny) {
+    SkinnyParams sp;
+    static_cast<QuantParams&>(sp) = p;
+    sp.stages = sk_stages;
+    sp.a_region = sk_region;
+    sp.a_grouped = grouped ? 1 : 0;
+    if (bn == 64) return qin ? dispatch_skinny<64, true>(epilogue, vec, maps, sp, grid, s)
+                             : dispatch_skinny<64, false>(epilogue, vec, maps, sp, grid, s);
+    return qin ? dispatch_skinny<128, true>(epilogue, vec, maps, sp, grid, s)
+               : dispatch_skinny<128, false>(epilogue, vec, maps, sp, grid, s);
+  }
   if (qin != nullptr) return dispatch_epi<64, false, true>(epilogue, vec, maps, p, grid, s);
   if (bn == 64) return dispatch_epi<64>(epilogue, vec, maps, p, grid, s);
   if (bn == 128) return dispatch_epi<128>(epilogue, vec, maps, p, grid, s);
