@@ -453,6 +453,7 @@ def run_gemm_configs(args, world, rank, local):
     g = torch.Generator(device=dev)
     g.manual_seed(0)
     wl = args.workload
+    calls = set(args.calls.split(","))
     if wl == "fc1":
         shapes = [("fc1", 1500, 5120, 1280, "none")]
     elif wl == "layer":
@@ -524,18 +525,22 @@ def run_gemm_configs(args, world, rank, local):
                            amax_ws=st.ws)
 
         reps = max(20, copies)
-        ms = _graph_time(gemm, args.steps, args.warmup, reps=reps)
-        qms = _graph_time(quant, args.steps, args.warmup, reps=reps)
-        bms = _graph_time(both, args.steps, args.warmup, reps=reps)
-        lms = _graph_time(linear, args.steps, args.warmup, reps=reps) if wl == "decoder" else None
+        timed = lambda f, what: _graph_time(f, args.steps, args.warmup, reps=reps) if what in calls else None  # noqa
+        ms = timed(gemm, "gemm")
+        qms = timed(quant, "quantise")
+        bms = timed(both, "both")
+        lms = timed(linear, "linear") if wl == "decoder" else None
         flops = 2.0 * M * N * K
         # decoder-step algorithmic bytes: 2MK (A fp16, quantised in-call) + NK (W fp8) + 2N (bias) + 2MN (out)
         dec_bytes = 2 * M * K + N * K + 2 * N + 2 * M * N
-        results[name] = {"M": M, "N": N, "K": K, "epilogue": epi, "operand_copies": copies,
-                         "gemm_ms": ms, "tflops": flops / ms / 1e9,
-                         "gemm_gbs_fp8_operands": (M * K + N * K + 2 * N + 2 * M * N) / ms / 1e6,
-                         "quantise_A_ms": qms, "quantise_A_gbs": 3 * M * K / qms / 1e6,
-                         "quantise_plus_gemm_ms": bms, "quantise_plus_gemm_gbs": dec_bytes / bms / 1e6}
+        results[name] = {"M": M, "N": N, "K": K, "epilogue": epi, "operand_copies": copies}
+        if ms is not None:
+            results[name].update({"gemm_ms": ms, "tflops": flops / ms / 1e9,
+                                  "gemm_gbs_fp8_operands": (M * K + N * K + 2 * N + 2 * M * N) / ms / 1e6})
+        if qms is not None:
+            results[name].update({"quantise_A_ms": qms, "quantise_A_gbs": 3 * M * K / qms / 1e6})
+        if bms is not None:
+            results[name].update({"quantise_plus_gemm_ms": bms, "quantise_plus_gemm_gbs": dec_bytes / bms / 1e6})
         if lms is not None:
             results[name].update({"linear_fp8_ms": lms, "linear_fp8_gbs": dec_bytes / lms / 1e6})
         if epi == "bias_maxkey":
@@ -549,9 +554,9 @@ def run_gemm_configs(args, world, rank, local):
         if name.endswith("_gelu_epilogue"):
             continue
         tot_flops += flops
-        tot_ms += ms
+        tot_ms += ms if ms is not None else float("nan")
         tot_bytes += dec_bytes
-        tot_dec_ms += bms if lms is None else lms
+        tot_dec_ms += lms if lms is not None else (bms if bms is not None else float("nan"))
     if wl == "decoder":
         value = tot_bytes / tot_dec_ms / 1e6
         line = {"metric": "decoder-step FP8 linear HBM GB/s (quantise A in-call + GEMM, 4 shapes)", "value": value,
@@ -622,6 +627,8 @@ def main():
                     default="stack")
     ap.add_argument("--chunks", type=int, default=64, help="batch of the attention workload")
     ap.add_argument("--shapes", default="", help="comma-separated shape names to keep (gemm workloads; for profiling)")
+    ap.add_argument("--calls", default="gemm,quantise,both,linear",
+                    help="gemm workloads: which timings to run (gemm, quantise, both, linear; for profiling)")
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--cpu-budget", type=float, default=20.0)
     ap.add_argument("--ref-step-budget", type=float, default=8.0)
