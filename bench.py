@@ -212,6 +212,20 @@ def cpu_reference_chunk(cfg, layers_fp16, budget_s: float) -> dict:
     return ref_encoder.time_cpu_chunk(qlayers, cfg.seq_len, cfg.d_model, cfg.heads, cfg.layers, budget_s=budget_s)
 
 
+def cpu_linear_seconds(x16: torch.Tensor, wq: torch.Tensor, w_scale: float, bias, residual, epi: str) -> float:
+    """Seconds of one call of the reference's CPU path for an FP8 linear on the host cores:
+    quantise the fp16 activation, fp32-dequantise both operands, fp32 matmul + bias +
+    epilogue, fp16 result (oracle/fp8.py, oracle/gemm.py). Operands are CPU tensors."""
+    from oracle import fp8 as ref_fp8
+    from oracle import gemm as ref_gemm
+    epi_code = {"none": ref_gemm.EPI_NONE, "gelu": ref_gemm.EPI_GELU, "residual": ref_gemm.EPI_RESIDUAL,
+                "residual_clamp": ref_gemm.EPI_RESIDUAL_CLAMP, "bias_maxkey": ref_gemm.EPI_NONE}[epi]
+    t0 = time.perf_counter()
+    aq, sa = ref_fp8.quantise_torch(x16)
+    ref_gemm.gemm_fp8_ref_f32(aq, float(sa), wq, w_scale, bias, residual, epi_code).half()
+    return time.perf_counter() - t0
+
+
 def cpu_layers(cfg, n_distinct: int = 2):
     """Distinct random layers for the CPU path (cycled through the 32 layers: the
     arithmetic per layer does not depend on which random weights it holds)."""
@@ -476,6 +490,10 @@ def run_gemm_configs(args, world, rank, local):
     hbm = measured_peaks()["hbm_gbs"]
     results = {}
     tot_flops = tot_ms = tot_bytes = tot_dec_ms = 0.0
+    cpu_on = rank == 0 and world == 1 and not args.no_cpu_baseline
+    cpu_s = cpu_flops = cpu_bytes = 0.0
+    if cpu_on:
+        torch.set_num_threads(len(os.sched_getaffinity(0)))
     l2_bytes = 126e6
     for name, M, N, K, epi in shapes:
         x = torch.randn(M, K, generator=g, device=dev).half()
@@ -553,6 +571,16 @@ def run_gemm_configs(args, world, rank, local):
             results["fc1_gelu_quantise"] = {"M": M, "N": N, "ms": gms, "gbs": 3 * M * N / gms / 1e6}
         if name.endswith("_gelu_epilogue"):
             continue
+        if cpu_on:  # the reference's CPU path on the same operands: one warm-up, one timed call
+            xc, wc, sw_c = x.cpu(), wq.cpu(), float(sw.item())
+            bc = b.cpu()
+            rc = None if res is None else res.cpu()
+            cpu_linear_seconds(xc, wc, sw_c, bc, rc, epi)
+            t_cpu = cpu_linear_seconds(xc, wc, sw_c, bc, rc, epi)
+            results[name]["cpu_ms"] = t_cpu * 1e3
+            cpu_s += t_cpu
+            cpu_flops += flops
+            cpu_bytes += dec_bytes
         tot_flops += flops
         tot_ms += ms if ms is not None else float("nan")
         tot_bytes += dec_bytes
@@ -571,6 +599,13 @@ def run_gemm_configs(args, world, rank, local):
                 "roofline": {"bound": "tensor", "achieved": value, "peak": peak_t, "unit": "TFLOP/s",
                              "frac": value / peak_t, "peak_source": src_t,
                              "frac_of_nominal_fp8_4500": value / NOMINAL_FP8_TFLOPS}}
+    if cpu_on and cpu_s > 0:
+        line["cpu_baseline"] = {
+            "value": (cpu_bytes / cpu_s / 1e9) if wl == "decoder" else (cpu_flops / cpu_s / 1e12),
+            "unit": line["unit"], "cores": torch.get_num_threads(), "kind": "port",
+            "sample": "one call per shape (after one warm-up) of the reference's CPU path on the same operands: "
+                      "quantise the fp16 activation, fp32-dequantise both operands, fp32 matmul + bias + "
+                      "epilogue, fp16 out (oracle/fp8.py quantise_torch, oracle/gemm.py)"}
     line.update({"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
                  "dtype": "fp8 e4m3", "data": "synthetic",
                  "timing": "CUDA graph of max(20, copies) back-to-back calls rotating over operand copies "
