@@ -62,3 +62,36 @@ def test_patch_without_layernorms():
     counts = patch_layers(m, full_fp16(), layernorms=False)
     assert counts["patched_layernorms"] == 0
     assert isinstance(m.encoder.layer_norm, torch.nn.LayerNorm)
+
+
+def test_stacked_cross_kv_runs_one_projection_per_input():
+    """k_proj / v_proj halves of a StackedKVProjection: one stacked linear per input tensor,
+    the halves equal the separate projections, the cache is released once both were served
+    and an in-place change of the input between the halves forces a new projection."""
+    import torch.nn as nn
+    from whisper_blaze_b200.modules import StackedKVProjection
+    from whisper_blaze_b200.precision import LayerPrecision
+    torch.manual_seed(0)
+    lin_k, lin_v = nn.Linear(64, 48, bias=False), nn.Linear(64, 40)
+    kv = StackedKVProjection(lin_k, lin_v, LayerPrecision())  # fp16 precision: the F.linear branch
+    calls = []
+    orig = kv.linear.forward
+    kv.linear.forward = lambda x: (calls.append(x.shape), orig(x))[1]
+    k_half, v_half = kv.half(0), kv.half(1)
+    x = torch.randn(2, 10, 64)
+    with torch.no_grad():
+        k, v = k_half(x), v_half(x)
+        assert len(calls) == 1 and kv._cache is None
+        assert k.shape == (2, 10, 48) and v.shape == (2, 10, 40)
+        torch.testing.assert_close(k, lin_k(x), rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(v, lin_v(x), rtol=1e-5, atol=1e-5)
+        k.view(2, -1, 6, 8)  # HF views the half per head; a strided half must allow it
+        x2 = x.clone()
+        k_half(x2), v_half(x2)
+        assert len(calls) == 2
+        x3 = torch.randn(2, 10, 64)
+        k_half(x3)
+        x3.add_(1.0)  # modified in place between the two halves
+        v3 = v_half(x3)
+        assert len(calls) == 4  # the k half's projection, then a new one for the changed input
+        torch.testing.assert_close(v3, lin_v(x3), rtol=1e-5, atol=1e-5)

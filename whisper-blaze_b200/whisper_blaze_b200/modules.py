@@ -8,6 +8,7 @@ BlazeLayerNorm mirrors model.py:116-168 unchanged in behaviour.
 """
 from __future__ import annotations
 
+import weakref
 from typing import Optional
 
 import torch
@@ -57,6 +58,60 @@ class BlazeLinear(nn.Module):
         self._w_fp8, self._w_scale = ops.quantise(w16, fmt)
         if self._has_bias:
             self._bias16 = self.bias.detach().to(w16.device, torch.float16).contiguous()
+
+
+class StackedKVProjection(nn.Module):
+    """A cross-attention layer's k_proj and v_proj as ONE FP8 linear.
+
+    The decoder's cross-attention projects the same encoder states twice, once
+    per generate call per layer. Here the two weights are stacked into one
+    [N_k + N_v, K] FP8 weight with one per-tensor scale (the stacked K/V shape
+    of config 4), and `half(0)` / `half(1)` are drop-in modules for k_proj and
+    v_proj: the first of them called on an input tensor runs the GEMM, the
+    other returns its half of the cached output (a strided view) if called on
+    the same, unmodified tensor; the cache is dropped once both halves were
+    served. Mirrors the two separate projections of HF's WhisperAttention
+    (cross-attention branch), whose results the stacked GEMM reproduces up to
+    the shared weight scale.
+    """
+
+    def __init__(self, k_proj: nn.Linear, v_proj: nn.Linear, layer_prec: LayerPrecision) -> None:
+        super().__init__()
+        if k_proj.in_features != v_proj.in_features:
+            raise ValueError("k_proj and v_proj must read the same input width")
+        self.n_k = k_proj.out_features
+        w = torch.cat([k_proj.weight.data.detach(), v_proj.weight.data.detach()], dim=0)
+        biases = []
+        for lin in (k_proj, v_proj):
+            biases.append(lin.bias.data.detach() if lin.bias is not None
+                          else torch.zeros(lin.out_features, dtype=lin.weight.dtype, device=lin.weight.device))
+        self.linear = BlazeLinear(w, torch.cat(biases), layer_prec)
+        self._cache = None  # (weakref to input, input version, output, halves served bitmask)
+
+    def project(self, x: torch.Tensor, which: int) -> torch.Tensor:
+        ent = self._cache
+        if ent is not None and ent[0]() is x and ent[1] == x._version:
+            out, served = ent[2], ent[3]
+        else:
+            out, served = self.linear(x), 0
+        served |= 1 << which
+        self._cache = None if served == 3 else (weakref.ref(x), x._version, out, served)
+        return out[..., :self.n_k] if which == 0 else out[..., self.n_k:]
+
+    def half(self, which: int) -> "StackedKVHalf":
+        return StackedKVHalf(self, which)
+
+
+class StackedKVHalf(nn.Module):
+    """k_proj (which=0) or v_proj (which=1) of a StackedKVProjection."""
+
+    def __init__(self, stacked: StackedKVProjection, which: int) -> None:
+        super().__init__()
+        object.__setattr__(self, "_stacked", stacked)  # owned (registered) by the attention module
+        self.which = which
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        return self._stacked.project(x, self.which)
 
 
 class BlazeLayerNorm(nn.Module):

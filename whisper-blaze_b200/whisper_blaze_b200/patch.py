@@ -13,6 +13,11 @@ BlazeLinear with the precision of its PrecisionConfig group
                        encoder_attn.*         -> decoder_cross_attn
                        fc1, fc2               -> decoder_ffn
 
+With an FP8 decoder_cross_attn group, each decoder layer's encoder_attn.k_proj and
+v_proj are stacked into one FP8 linear (StackedKVProjection): the cross-attention
+K/V of a generate call is one GEMM of width 2 x d_model per layer (config 4's
+shape) instead of two.
+
 Layers are recognised by class name, so transformers is not imported here.
 A linear whose group is FP16 keeps the fp16 F.linear path of BlazeLinear
 (bit-identical to nn.Linear); an FP8 group quantises its weight once, on the
@@ -24,7 +29,7 @@ from typing import Dict, Optional
 
 import torch.nn as nn
 
-from .modules import BlazeLayerNorm, BlazeLinear
+from .modules import BlazeLayerNorm, BlazeLinear, StackedKVProjection
 from .precision import LayerPrecision, PrecisionConfig
 
 ENCODER_LAYER = "WhisperEncoderLayer"
@@ -60,18 +65,40 @@ def _set_child(root: nn.Module, path: str, new: nn.Module) -> None:
     setattr(parent, leaf, new)
 
 
-def patch_layers(model: nn.Module, precision: PrecisionConfig, layernorms: bool = True) -> Dict[str, int]:
+def patch_layers(model: nn.Module, precision: PrecisionConfig, layernorms: bool = True,
+                 stack_cross_kv: bool = True) -> Dict[str, int]:
     """Swap the linears (by precision group) and, optionally, the LayerNorms of `model` in place.
 
-    Returns counts: patched_layernorms, patched_linears and one entry per group that
-    received at least one FP8 linear (``fp8_<group>``).
+    With stack_cross_kv and an FP8 decoder_cross_attn group, each decoder layer's
+    encoder_attn.k_proj / v_proj become the two halves of one StackedKVProjection
+    (registered as encoder_attn.kv_proj): one FP8 GEMM of width 2 x d_model per
+    generate call and layer instead of two.
+
+    Returns counts: patched_layernorms, patched_linears (k and v count as two),
+    stacked_cross_kv, and one entry per group that received at least one FP8
+    linear (``fp8_<group>``).
     """
-    counts: Dict[str, int] = {"patched_layernorms": 0, "patched_linears": 0}
+    counts: Dict[str, int] = {"patched_layernorms": 0, "patched_linears": 0, "stacked_cross_kv": 0}
     for layer in list(model.modules()):
         kind = type(layer).__name__
         if kind not in (ENCODER_LAYER, DECODER_LAYER):
             continue
+        stacked_paths = set()
+        xattn = getattr(layer, "encoder_attn", None) if kind == DECODER_LAYER else None
+        if (stack_cross_kv and xattn is not None and precision.decoder_cross_attn.is_fp8()
+                and isinstance(getattr(xattn, "k_proj", None), nn.Linear)
+                and isinstance(getattr(xattn, "v_proj", None), nn.Linear)):
+            kv = StackedKVProjection(xattn.k_proj, xattn.v_proj, precision.decoder_cross_attn)
+            xattn.kv_proj = kv
+            xattn.k_proj = kv.half(0)
+            xattn.v_proj = kv.half(1)
+            stacked_paths = {"encoder_attn.k_proj", "encoder_attn.v_proj"}
+            counts["patched_linears"] += 2
+            counts["stacked_cross_kv"] += 1
+            counts["fp8_decoder_cross_attn"] = counts.get("fp8_decoder_cross_attn", 0) + 2
         for path, child in list(layer.named_modules()):
+            if path in stacked_paths or path.startswith("encoder_attn.kv_proj"):
+                continue
             if not isinstance(child, nn.Linear):
                 continue
             group = linear_group(kind, path)
