@@ -175,12 +175,13 @@ __device__ __forceinline__ void split_range(const Params& p, int g, int split, i
 }
 
 // Grid-wide arrival for the cooperatively launched (all CTAs co-resident)
-// in-kernel quantise: publishes this CTA's earlier global writes, counts it in
-// *count, and waits until all `expected` CTAs have arrived. Bounded: gives up
-// after `timeout_ns` of wall clock, recording the error.
+// in-kernel quantise, run by one thread per CTA after a __syncthreads: a
+// release add counts the CTA in *count (release is cumulative, so it also
+// publishes the CTA's global writes that the barrier ordered before it), then
+// an acquire poll waits until all `expected` CTAs have arrived. Bounded: gives
+// up after `timeout_ns` of wall clock, recording the error.
 __device__ __noinline__ bool grid_arrive_wait(uint32_t* count, uint32_t expected, uint64_t timeout_ns) {
-  __threadfence();
-  atomicAdd(count, 1u);
+  asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(count) : "memory");
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t it = 0; it < (1u << 30); ++it) {
     uint32_t v;
@@ -248,7 +249,6 @@ __device__ __forceinline__ bool quantise_a_prologue(const QuantParams& p, QuantS
                         : make_uint2(q8x4<WBK_FMT_E4M3>(v.x, v.y, inv, mx), q8x4<WBK_FMT_E4M3>(v.z, v.w, inv, mx));
     }
     fence_async_global();  // the codes are read back by TMA (async proxy), in other CTAs too
-    __threadfence();
   }
   __syncthreads();
   if (threadIdx.x == kQuantLeader && q.ok) {
