@@ -458,6 +458,9 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
   const uint32_t tmem_base = s.tmem_base;
   // Launched with programmatic stream serialization: everything above overlaps
   // the kernel that produces A / the scales; nothing below runs before it is done.
+  // A following kernel launched the same way may start its own prologue on SMs
+  // this grid leaves free (its wait still blocks until this grid has finished).
+  griddep_launch_dependents();
   griddep_wait();
 
   // TMA loads of one single-CTA stage: the A and/or W boxes of K blocks [kb, kb + G).
@@ -960,6 +963,7 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = h.tmem_base;
+  griddep_launch_dependents();  // as in fp8_gemm_kernel
   griddep_wait();
 
   // W boxes of K blocks [kb, kb + G) of the tile at column n0 into ring stage `st`.
@@ -1271,11 +1275,16 @@ bool pdl_enabled() {
 }
 
 // Programmatic dependent launch for the cooperative (in-kernel quantise)
-// variant too (default off; WBK_PDL_COOP=1 turns it on).
+// variant too (default on; WBK_PDL_COOP=0 turns it off). A dependent grid can
+// only launch once every CTA of the grid before it has started (and signalled),
+// so that grid is wholly resident; the dependent's CTAs that find room wait in
+// griddepcontrol.wait until it has finished, and the rest launch as its CTAs
+// exit, so all of them are resident before any passes the wait. Measured on
+// B200: the decoder-step linears 0.5 - 0.8 us shorter each.
 bool pdl_coop_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("WBK_PDL_COOP");
-    return e != nullptr && std::atoi(e) != 0;
+    return !(e && e[0] == '0');
   }();
   return on;
 }
