@@ -912,6 +912,11 @@ struct SkinnyParams : QuantParams {
   int stages;           // weight ring depth
   uint32_t a_region;    // bytes of the resident A region (K blocks x 8 KB + slack), 1024-multiple
   int a_grouped;        // 1: one 3-D box brings all of A
+  // Work items: items [0, full_items) are whole kBN-wide tiles; the columns past
+  // them are split into kBN/2-wide items, so a last partial round of whole tiles
+  // becomes one round of half tiles on up to twice as many CTAs.
+  int full_items;
+  uint32_t idesc_half;  // instruction descriptor of the kBN/2-wide MMA
 };
 
 // Dynamic shared memory of a skinny launch.
@@ -923,8 +928,10 @@ template <int kBN, int kEpi, bool kTmaStore, bool kQuantA>
 __global__ void __launch_bounds__(THREADS, 1)
 fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_a3,
-                  const __grid_constant__ CUtensorMap tmap_w3, const SkinnyParams p) {
+                  const __grid_constant__ CUtensorMap tmap_w3, const __grid_constant__ CUtensorMap tmap_wh,
+                  const SkinnyParams p) {
   using SK = Skinny<kBN>;
+  constexpr int kHalf = kBN / 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   SkinnyHeader& h = *reinterpret_cast<SkinnyHeader*>(base);
@@ -966,14 +973,20 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   griddep_launch_dependents();  // as in fp8_gemm_kernel
   griddep_wait();
 
-  // W boxes of K blocks [kb, kb + G) of the tile at column n0 into ring stage `st`.
-  auto load_w = [&](int st, int kb, int n0) {
+  // Item t: first column and whether it is a half-width tile.
+  auto item_n0 = [&](int t) { return t < p.full_items ? t * kBN : p.full_items * kBN + (t - p.full_items) * kHalf; };
+  // W boxes of K blocks [kb, kb + G) of the item at column n0 into ring stage `st`
+  // (kBN rows, or kBN/2 rows for a half item, stacked per K block).
+  auto load_w = [&](int st, int kb, int n0, bool half) {
     uint8_t* dst = b_smem + static_cast<size_t>(st) * SK::B_STAGE;
+    mbar_arrive_expect_tx(&h.full[st], half ? SK::B_STAGE / 2 : SK::B_STAGE);
     if (p.grouped) {
-      tma_load_3d(&tmap_w3, &h.full[st], dst, 0, n0, kb);
+      tma_load_3d(half ? &tmap_wh : &tmap_w3, &h.full[st], dst, 0, n0, kb);
     } else {
+      const int rows = half ? kHalf : kBN;
 #pragma unroll
-      for (int g = 0; g < SK::G; ++g) tma_load_2d(&tmap_w, &h.full[st], dst + g * kBN * BK, (kb + g) * BK, n0);
+      for (int g = 0; g < SK::G; ++g)
+        tma_load_2d(half ? &tmap_wh : &tmap_w, &h.full[st], dst + g * rows * BK, (kb + g) * BK, n0);
     }
   };
   // All of A (every K block, 64-row boxes) into the resident region, two K blocks
@@ -996,8 +1009,7 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
   if constexpr (kQuantA) {
     run = quantise_a_prologue(p, h.q, [&]() {
       for (int t = blockIdx.x, kb = 0; t < p.num_tiles && pre < stages; ++pre) {
-        mbar_arrive_expect_tx(&h.full[pre], SK::B_STAGE);
-        load_w(pre, kb, t * kBN);
+        load_w(pre, kb, item_n0(t), t >= p.full_items);
         kb += SK::G;
         if (kb >= p.kblocks) {
           kb = 0;
@@ -1026,15 +1038,15 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
       int n_st = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int n0 = tile * kBN;
+        const int n0 = item_n0(tile);
+        const bool half = tile >= p.full_items;
         for (int kb = 0; kb < p.kblocks; kb += SK::G) {
           if (!(kQuantA && n_st < pre)) {
             if (!mbar_wait(&h.empty[st], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&h.full[st], SK::B_STAGE);
-            load_w(st, kb, n0);
+            load_w(st, kb, n0, half);
           }
           ++n_st;
           if (++st == stages) {
@@ -1075,6 +1087,9 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
           break;
         }
         tc_fence_after();
+        const bool half = tile >= p.full_items;
+        const uint32_t idesc = half ? p.idesc_half : p.idesc;
+        const int b_rows = half ? kHalf : kBN;
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kBN);
         for (int kbs = 0; kbs < p.kblocks; kbs += SK::G) {
           if (!mbar_wait(&h.full[st], phase, abort_flag, p.timeout_ns, SITE_MMA_FULL)) {
@@ -1095,11 +1110,11 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
             const int kb = kbs + g;
             if (kb >= p.kblocks) break;
             const uint64_t adesc = make_sw128_desc(a_smem + kb * kSkABlock);
-            const uint64_t bdesc = make_sw128_desc(bst + g * kBN * BK);
+            const uint64_t bdesc = make_sw128_desc(bst + g * b_rows * BK);
 #pragma unroll
             for (int k = 0; k < BK / UMMA_K; ++k) {
               const uint64_t koff = static_cast<uint64_t>((k * UMMA_K) >> 4);
-              umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > 0 || k > 0) ? 1u : 0u);
+              umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, idesc, (kb > 0 || k > 0) ? 1u : 0u);
             }
           }
           umma_commit(&h.empty[st]);
@@ -1136,14 +1151,16 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
     const int row0 = quarter * 32;
     const int row = row0 + lane;
     for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-      const int n0 = tile * kBN + col_half * SK::EPI_COLS;
+      const int item0 = item_n0(tile);
+      const int item_end = min(p.N, item0 + (tile >= p.full_items ? kHalf : kBN));
+      const int n0 = item0 + col_half * SK::EPI_COLS;
       uint4 resa[4], resb[4];
       prefetch_residual<kEpi, kTmaStore>(p, row, n0, resa);
       if (!mbar_wait(&h.acc_full[acc], acc_phase, abort_flag, p.timeout_ns, SITE_EPI_ACC_FULL)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(acc * kBN + col_half * SK::EPI_COLS);
-      const int nchunks = min(SK::EPI_COLS / CHUNK, (p.N - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
+      const int nchunks = min(SK::EPI_COLS / CHUNK, (item_end - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
       auto process = [&](const uint32_t* regs, const uint4* res, int c) {
         const int col0 = n0 + c * CHUNK;
         float v[32];
@@ -1370,7 +1387,17 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
 
 struct Maps {
   CUtensorMap a, w, out, a3, w3;
+  CUtensorMap wh;  // skinny kernel: the weight box of a half-width item
 };
+
+// Half-width items in the skinny kernel's last round (default on; WBK_GEMM_HALF_TILES=0 turns them off).
+bool half_items_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_GEMM_HALF_TILES");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 // Skinny kernel for M <= 64, K <= 1536 (default on; WBK_GEMM_SKINNY=0 uses the general kernel).
 bool skinny_enabled() {
@@ -1417,7 +1444,7 @@ int launch_skinny(const Maps& m, const SkinnyParams& p, int grid, cudaStream_t s
   }
   cfg.attrs = attr;
   cfg.numAttrs = nattr;
-  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, m.a, m.w, m.out, m.a3, m.w3, p), "fp8 skinny gemm launch");
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, m.a, m.w, m.out, m.a3, m.w3, m.wh, p), "fp8 skinny gemm launch");
 }
 
 template <int kBN, bool kQuantA>
@@ -1821,6 +1848,28 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
     sp.stages = sk_stages;
     sp.a_region = sk_region;
     sp.a_grouped = grouped ? 1 : 0;
+    // Half-width items for the last round when whole tiles would leave part of it
+    // idle: e.g. 811 tiles on 148 CTAs (71 CTAs with a sixth tile) become 740
+    // whole tiles and 141 half tiles, one each on 141 CTAs.
+    sp.full_items = sp.num_tiles;
+    sp.idesc_half = (p.idesc & ~(0x3Fu << 17)) | (static_cast<uint32_t>((bn / 2) >> 3) << 17);
+    maps.wh = maps.w3;  // unused unless there are half items
+    if (sp.num_tiles > grid && sp.num_tiles % grid != 0 && half_items_enabled()) {
+      const int full = (sp.num_tiles / grid) * grid;
+      const int64_t rest = N - static_cast<int64_t>(full) * bn;
+      const int halves = static_cast<int>((rest + bn / 2 - 1) / (bn / 2));
+      if (halves <= grid) {
+        const uint32_t half_rows = static_cast<uint32_t>(bn / 2);
+        const int e = grouped ? make_tmap_kblocks(&maps.wh, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                                                  half_rows, static_cast<uint32_t>(Skinny<64>::G))
+                              : make_tmap(&maps.wh, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, K, N, BK, half_rows,
+                                          CU_TENSOR_MAP_SWIZZLE_128B);
+        if (e != WBK_OK) return e;
+        sp.full_items = full;
+        sp.num_tiles = full + halves;
+        sp.num_items = sp.num_tiles;
+      }
+    }
     if (bn == 64) return qin ? dispatch_skinny<64, true>(epilogue, vec, maps, sp, grid, s)
                              : dispatch_skinny<64, false>(epilogue, vec, maps, sp, grid, s);
     return qin ? dispatch_skinny<128, true>(epilogue, vec, maps, sp, grid, s)
