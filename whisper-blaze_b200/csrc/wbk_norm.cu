@@ -229,9 +229,13 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
   };
   const int64_t stride = static_cast<int64_t>(gridDim.x) * kWarps;
   int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  // The quantise pass visits rows last to first: the statistics pass that ran
+  // just before read them first to last, so the rows still in L2 come first.
+  auto phys = [&](int64_t r) { return kMode == kModeQuant ? rows - 1 - r : r; };
   auto row_ptrs = [&](int64_t r, const uint4*& xr, const uint4*& rr) {
-    xr = reinterpret_cast<const uint4*>(x + r * D);
-    rr = res ? reinterpret_cast<const uint4*>(res + r * D) : nullptr;
+    const int64_t pr = phys(r);
+    xr = reinterpret_cast<const uint4*>(x + pr * D);
+    rr = res ? reinterpret_cast<const uint4*>(res + pr * D) : nullptr;
   };
   uint4 xa[kVpl], ra[kVpl], xb[kVpl], rb[kVpl];
   const uint4 *xr, *rr;
@@ -239,7 +243,7 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
     for (; row < rows; row += stride) {
       row_ptrs(row, xr, rr);
       load_row_raw<kVpl, kRes>(xr, rr, lane, nvec, xa, ra);
-      process_row(row, xa, ra);
+      process_row(phys(row), xa, ra);
     }
   } else {
     if (row < rows) {
@@ -252,7 +256,7 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
         row_ptrs(next, xr, rr);
         load_row_raw<kVpl, kRes>(xr, rr, lane, nvec, xb, rb);
       }
-      process_row(row, xa, ra);
+      process_row(phys(row), xa, ra);
       row = next;
       if (row >= rows) break;
       next = row + stride;
@@ -260,7 +264,7 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
         row_ptrs(next, xr, rr);
         load_row_raw<kVpl, kRes>(xr, rr, lane, nvec, xa, ra);
       }
-      process_row(row, xb, rb);
+      process_row(phys(row), xb, rb);
       row = next;
     }
   }

@@ -34,6 +34,7 @@ template <bool kVec>
 __global__ void __launch_bounds__(kThreads)
 amax_f16_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ amax_bits) {
   uint32_t m = 0;  // two packed running maxima
+  const uint64_t keep = l2_policy_evict_last();  // the quantise pass re-reads these lines
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   int64_t done = 0;
@@ -42,10 +43,10 @@ amax_f16_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ 
     const uint4* xv = reinterpret_cast<const uint4*>(x);
     int64_t i = tid;
     for (; i + 3 * stride < nvec; i += 4 * stride) {
-      const uint4 v0 = ld_stream16(xv + i);
-      const uint4 v1 = ld_stream16(xv + i + stride);
-      const uint4 v2 = ld_stream16(xv + i + 2 * stride);
-      const uint4 v3 = ld_stream16(xv + i + 3 * stride);
+      const uint4 v0 = ld_stream16_hint(xv + i, keep);
+      const uint4 v1 = ld_stream16_hint(xv + i + stride, keep);
+      const uint4 v2 = ld_stream16_hint(xv + i + 2 * stride, keep);
+      const uint4 v3 = ld_stream16_hint(xv + i + 3 * stride, keep);
       m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v0.x), abs2_nonan(v0.y)),
                                __vmaxu2(abs2_nonan(v0.z), abs2_nonan(v0.w))));
       m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v1.x), abs2_nonan(v1.y)),
@@ -56,7 +57,7 @@ amax_f16_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ 
                                __vmaxu2(abs2_nonan(v3.z), abs2_nonan(v3.w))));
     }
     for (; i < nvec; i += stride) {
-      const uint4 v = ld_stream16(xv + i);
+      const uint4 v = ld_stream16_hint(xv + i, keep);
       m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v.x), abs2_nonan(v.y)),
                                __vmaxu2(abs2_nonan(v.z), abs2_nonan(v.w))));
     }
@@ -96,16 +97,23 @@ quantise_f16_kernel(const __half* __restrict__ x, int64_t n, const uint32_t* __r
     const int64_t nvec = n >> 3;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
     uint2* qv = reinterpret_cast<uint2*>(q);
-    int64_t i = tid;
-    for (; i + stride < nvec; i += 2 * stride) {
-      const uint4 v0 = ld_stream16(xv + i);
-      const uint4 v1 = ld_stream16(xv + i + stride);
-      qv[i] = make_uint2(q8x4<kFmt>(v0.x, v0.y, inv, max_fp8), q8x4<kFmt>(v0.z, v0.w, inv, max_fp8));
-      qv[i + stride] = make_uint2(q8x4<kFmt>(v1.x, v1.y, inv, max_fp8), q8x4<kFmt>(v1.z, v1.w, inv, max_fp8));
+    // Grid-stride rounds from the LAST to the first: the amax pass that ran just
+    // before read the tensor front to back, so its most recent lines -- the ones
+    // still in L2 -- are read first here. Only the order changes.
+    const int64_t rounds = (nvec + stride - 1) / stride;
+    const uint64_t drop = l2_policy_evict_first();  // last use of the input
+    int64_t r = rounds - 1;
+    for (; r >= 1; r -= 2) {  // rounds r and r - 1 (r - 1 < rounds - 1 is a full round)
+      const int64_t i0 = r * stride + tid, i1 = i0 - stride;
+      const bool has0 = i0 < nvec;
+      const uint4 v0 = has0 ? ld_stream16_hint(xv + i0, drop) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 v1 = ld_stream16_hint(xv + i1, drop);
+      if (has0) qv[i0] = make_uint2(q8x4<kFmt>(v0.x, v0.y, inv, max_fp8), q8x4<kFmt>(v0.z, v0.w, inv, max_fp8));
+      qv[i1] = make_uint2(q8x4<kFmt>(v1.x, v1.y, inv, max_fp8), q8x4<kFmt>(v1.z, v1.w, inv, max_fp8));
     }
-    for (; i < nvec; i += stride) {
-      const uint4 v = ld_stream16(xv + i);
-      qv[i] = make_uint2(q8x4<kFmt>(v.x, v.y, inv, max_fp8), q8x4<kFmt>(v.z, v.w, inv, max_fp8));
+    if (r == 0 && tid < nvec) {
+      const uint4 v = ld_stream16_hint(xv + tid, drop);
+      qv[tid] = make_uint2(q8x4<kFmt>(v.x, v.y, inv, max_fp8), q8x4<kFmt>(v.z, v.w, inv, max_fp8));
     }
     done = nvec << 3;
   }
