@@ -281,3 +281,25 @@ def test_skinny_kernel_matches_general_kernel(cuda_device, tmp_path):
         assert torch.equal(q.cpu(), qg) and torch.equal(s.cpu(), sg), (M, N, K)
         assert torch.equal(y.cpu().view(torch.int16), yg.view(torch.int16)), (M, N, K, "linear")
         assert torch.equal(y2.cpu().view(torch.int16), y2g.view(torch.int16)), (M, N, K, "gemm")
+
+
+@pytest.mark.parametrize("M,N,K", [(1500, 5120, 1280), (64, 1280, 1280), (300, 1000, 1296)])
+def test_gemm_vs_reference_gpu_linear_path(cuda_device, M, N, K):
+    """Against the reference's own GPU path for an FP8 linear (BlazeLinear.forward,
+    whisper_blaze/model.py:80-109): quantise x, dequantise both operands to fp16
+    (dequantise_e4m3, bit-identical to the reference kernel), then F.linear (cuBLAS fp16).
+    The operands differ only by the fp16 rounding of the dequantised values, so the
+    north-star gate (max relative error <= 1e-2) applies; the error is printed."""
+    import whisper_blaze_kernels as K_
+    x = randn_f16((M, K), 91 + M).to(cuda_device)
+    w = randn_f16((N, K), 92 + N, std=0.02).to(cuda_device)
+    b = randn_f16((N,), 93, std=0.02).to(cuda_device)
+    aq, sa = K_.quantise_e4m3(x)
+    wq, sw = K_.quantise_e4m3(w)
+    a16 = K_.dequantise_e4m3(aq, sa, [M, K])
+    w16 = K_.dequantise_e4m3(wq, sw, [N, K])
+    y_ref_path = torch.nn.functional.linear(a16, w16, b).float()
+    y = ops.gemm_fp8(aq, sa, wq, sw, b).float()
+    rel = ((y - y_ref_path).abs().max() / y_ref_path.abs().max()).item()
+    print(f"\nFP8 GEMM vs reference GPU path (fp16 dequantise + cuBLAS) {M}x{N}x{K}: max relative error {rel:.3e}")
+    assert rel <= REL_GATE
