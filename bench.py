@@ -1,7 +1,7 @@
 """Benchmark of the B200 FP8 quantised-matmul path (whisper-blaze north star).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload stack|layer|fc1|decoder|crossattn]
+                    [--workload stack|layer|fc1|decoder|crossattn|attention|norms]
 
 Default workload (config 5 of the north star): a 32-layer Whisper-large-v3
 encoder stack (d_model 1280, 20 heads, FFN 5120, pre-LN, every linear FP8
@@ -25,7 +25,8 @@ on one chunk on all host cores.
 
 Secondary workloads print their own line with their
 own metric: fc1 (config 1), layer (config 2), decoder (config 3), crossattn
-(config 4).
+(config 4); attention (the encoder self-attention kernel against torch SDPA)
+and norms (the norm ops' HBM bandwidth) cover the other kernels.
 """
 from __future__ import annotations
 
@@ -652,13 +653,96 @@ def run_attention(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_norms(args, world, rank, local):
+    """The norm ops of the op surface at the stack's shape (96000 x 1280 fp16, gamma = 1, beta = 0),
+    HBM-bound: layernorm_fused, layernorm_fused_residual (normed + sum), rmsnorm_fused (with
+    residual) and the fused LayerNorm -> FP8 pair. Algorithmic bytes per call (the LayerNorm rule):
+    2 R D (1 + has_res + 1 + want_sum) + 2 D per parameter vector; LayerNorm -> FP8: 2 R D in +
+    R D codes out. Each timing is a CUDA graph rotating over three inputs (each > the 126 MB L2)."""
+    from whisper_blaze_b200 import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    R, D = TOTAL_CHUNKS * 1500, 1280
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    xs = [torch.randn(R, D, generator=g, device=dev).half() for _ in range(3)]
+    rs = [torch.randn(R, D, generator=g, device=dev).half() for _ in range(3)]
+    gamma = torch.ones(D, dtype=torch.float16, device=dev)
+    beta = torch.zeros(D, dtype=torch.float16, device=dev)
+    out = torch.empty(R, D, dtype=torch.float16, device=dev)
+    sm = torch.empty(R, D, dtype=torch.float16, device=dev)
+    q = torch.empty(R, D, dtype=torch.uint8, device=dev)
+    sc = torch.empty(1, dtype=torch.float32, device=dev)
+    ws = ops.layernorm_quantise_ws(R, dev)
+    am = ops.new_amax_ws(dev)
+    ctr = [0]
+
+    def nxt():
+        ctr[0] += 1
+        return ctr[0] % 3
+
+    cases = [
+        ("layernorm_fused", lambda: ops.layernorm(xs[nxt()], None, gamma, beta, out=out), 2 * R * D * 2 + 4 * D),
+        ("layernorm_fused_residual", lambda: (lambda i: ops.layernorm(xs[i], rs[i], gamma, beta, want_sum=True,
+                                                                       out=out, sum_out=sm))(nxt()),
+         2 * R * D * 4 + 4 * D),
+        ("rmsnorm_fused", lambda: (lambda i: ops.rmsnorm(xs[i], rs[i], gamma))(nxt()), 2 * R * D * 3 + 2 * D),
+        ("layernorm_quantise", lambda: ops.layernorm_quantise(xs[nxt()], gamma, beta, q_out=q, scale_out=sc, ws=ws,
+                                                               amax_ws=am), 3 * R * D + 4 * D),
+    ]
+    hbm = measured_peaks()["hbm_gbs"]
+    results, tot_b, tot_ms = {}, 0.0, 0.0
+    cpu_on = rank == 0 and world == 1 and not args.no_cpu_baseline
+    cpu_b = cpu_s = 0.0
+    if cpu_on:
+        torch.set_num_threads(len(os.sched_getaffinity(0)))
+        xc, rc_ = xs[0].cpu(), rs[0].cpu()
+        gc, bc = gamma.cpu().float(), beta.cpu().float()
+    for name, fn, nbytes in cases:
+        ms = _graph_time(fn, args.steps, args.warmup, reps=30)
+        results[name] = {"rows": R, "D": D, "us_per_call": ms * 1e3, "gbs": nbytes / ms / 1e6,
+                         "frac_of_hbm": nbytes / ms / 1e6 / hbm}
+        tot_b += nbytes
+        tot_ms += ms
+        if cpu_on:  # the reference's CPU path: torch fp32 layer_norm / rms norm of the same input
+            t0 = time.perf_counter()
+            xf = xc.float()
+            if name == "rmsnorm_fused":
+                h = xf + rc_.float()
+                (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-5) * gc).half()
+            elif name == "layernorm_fused_residual":
+                h = xf + rc_.float()
+                torch.nn.functional.layer_norm(h, [D], gc, bc, 1e-5).half()
+                h.half()
+            else:
+                torch.nn.functional.layer_norm(xf, [D], gc, bc, 1e-5).half()
+            t = time.perf_counter() - t0
+            results[name]["cpu_ms"] = t * 1e3
+            cpu_b += nbytes
+            cpu_s += t
+    value = tot_b / tot_ms / 1e6
+    line = {"metric": "norm ops HBM GB/s (layernorm_fused, _residual, rmsnorm_fused, LayerNorm->FP8; 96000 x 1280)",
+            "value": value, "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "fp16 (fp32 statistics)", "data": "synthetic",
+            "timing": "CUDA graph of 30 calls rotating over 3 inputs (each > the 126 MB L2), device time per call",
+            "roofline": {"bound": "hbm", "achieved": value, "peak": hbm, "unit": "GB/s", "frac": value / hbm,
+                         "peak_source": "hbm_gbs of MEASURED_PEAKS.json"},
+            "config": {"workload": "norms", "ops": results}}
+    if cpu_on and cpu_s > 0:
+        line["cpu_baseline"] = {"value": cpu_b / cpu_s / 1e9, "unit": "GB/s", "cores": torch.get_num_threads(),
+                                "kind": "port", "sample": "one call per op of torch-CPU fp32 layer_norm / rms norm "
+                                                          "on the same 96000 x 1280 input (fp16 out)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "layer", "fc1", "decoder", "crossattn", "attention"],
+    ap.add_argument("--workload", choices=["stack", "layer", "fc1", "decoder", "crossattn", "attention", "norms"],
                     default="stack")
     ap.add_argument("--chunks", type=int, default=64, help="batch of the attention workload")
     ap.add_argument("--shapes", default="", help="comma-separated shape names to keep (gemm workloads; for profiling)")
@@ -680,6 +764,8 @@ def main():
             run_stack(args, world, rank, local)
         elif args.workload == "attention":
             run_attention(args, world, rank, local)
+        elif args.workload == "norms":
+            run_norms(args, world, rank, local)
         else:
             run_gemm_configs(args, world, rank, local)
     finally:
