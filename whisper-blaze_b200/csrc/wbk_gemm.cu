@@ -885,13 +885,14 @@ constexpr int kSkEpiWarps = 4;                       // warps of lane quarters 0
 constexpr int kSkMaxKBlocks = 12;                    // K <= 1536
 constexpr int kSkStageOut = 2 * STAGE_OUT_BYTES;     // per active epilogue warp, double-buffered
 
-template <int kBN>
+// kG: K blocks per weight stage. 2 in general; 5 when K is a multiple of 640
+// (K = 1280: 40 KB boxes; a TMA probe streamed 40 KB boxes ~5 % faster than 16 KB ones).
+template <int kBN, int kG = 2>
 struct Skinny {
-  static constexpr int G = 2;                        // K blocks per weight stage
-  static constexpr int B_STAGE = G * kBN * BK;       // 16 KB (64-wide) / 32 KB (128-wide)
+  static constexpr int G = kG;
+  static constexpr int B_STAGE = G * kBN * BK;       // 16 / 40 KB (64-wide), 32 KB (128-wide)
   static constexpr int EPI_COLS = kBN / 2;           // columns per epilogue warp
   static constexpr int TMEM_COLS = NUM_ACC * kBN;
-  static_assert(G == 2, "A's barriers cover two K blocks each, one weight stage");
 };
 
 struct SkinnyHeader {  // at the (1024-aligned) start of shared memory
@@ -924,13 +925,13 @@ __host__ __device__ constexpr size_t skinny_smem(uint32_t a_region, int stages, 
   return 1024 + kSkHeaderBytes + a_region + static_cast<size_t>(stages) * b_stage + kSkEpiWarps * kSkStageOut;
 }
 
-template <int kBN, int kEpi, bool kTmaStore, bool kQuantA>
+template <int kBN, int kEpi, bool kTmaStore, bool kQuantA, int kG>
 __global__ void __launch_bounds__(THREADS, 1)
 fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                   const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_a3,
                   const __grid_constant__ CUtensorMap tmap_w3, const __grid_constant__ CUtensorMap tmap_wh,
                   const SkinnyParams p) {
-  using SK = Skinny<kBN>;
+  using SK = Skinny<kBN, kG>;
   constexpr int kHalf = kBN / 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -1081,6 +1082,7 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
       uint32_t acc_phase = 0;
       bool ok = true;
       bool a_ready = false;  // every A block landed (checked during the first tile)
+      int a_next = 0;        // next pair of A blocks whose barrier is still to be waited on
       for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
         if (!mbar_wait(&h.acc_empty[acc], acc_phase ^ 1u, abort_flag, p.timeout_ns, SITE_MMA_ACC_EMPTY)) {
           ok = false;
@@ -1096,12 +1098,12 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
             ok = false;
             break;
           }
-          if (!a_ready) {
-            if (!mbar_wait(&h.a_full[kbs >> 1], 0, abort_flag, p.timeout_ns, SITE_MMA_FULL)) {
-              ok = false;
-              break;
-            }
-            a_ready = kbs + SK::G >= p.kblocks;
+          if (!a_ready) {  // the A pairs this stage's K blocks need
+            const int jlast = (min(kbs + SK::G, p.kblocks) - 1) >> 1;
+            for (; a_next <= jlast && ok; ++a_next)
+              ok = mbar_wait(&h.a_full[a_next], 0, abort_flag, p.timeout_ns, SITE_MMA_FULL);
+            if (!ok) break;
+            a_ready = 2 * a_next >= p.kblocks;
           }
           tc_fence_after();
           const uint8_t* bst = b_smem + static_cast<size_t>(st) * SK::B_STAGE;
@@ -1390,6 +1392,16 @@ struct Maps {
   CUtensorMap wh;  // skinny kernel: the weight box of a half-width item
 };
 
+// Five-K-block weight stages in the skinny kernel where they divide K (default on;
+// WBK_SKINNY_G=2 keeps two-block stages).
+bool skinny_g5_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_SKINNY_G");
+    return !(e && e[0] == '2');
+  }();
+  return on;
+}
+
 // Half-width items in the skinny kernel's last round (default on; WBK_GEMM_HALF_TILES=0 turns them off).
 bool half_items_enabled() {
   static const bool on = [] {
@@ -1408,13 +1420,13 @@ bool skinny_enabled() {
   return on;
 }
 
-template <int kBN, int kEpi, bool kTma, bool kQuantA>
+template <int kBN, int kEpi, bool kTma, bool kQuantA, int kG>
 int launch_skinny(const Maps& m, const SkinnyParams& p, int grid, cudaStream_t stream) {
   static std::mutex mu;
   static std::vector<char> configured;
   const int dev = current_device();
   if (dev < 0) return fail(WBK_ERR_CUDA, "no current CUDA device");
-  auto kernel = fp8_skinny_kernel<kBN, kEpi, kTma, kQuantA>;
+  auto kernel = fp8_skinny_kernel<kBN, kEpi, kTma, kQuantA, kG>;
   {
     std::lock_guard<std::mutex> lock(mu);
     if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
@@ -1428,7 +1440,7 @@ int launch_skinny(const Maps& m, const SkinnyParams& p, int grid, cudaStream_t s
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
   cfg.blockDim = dim3(THREADS, 1, 1);
-  cfg.dynamicSmemBytes = skinny_smem(p.a_region, p.stages, Skinny<kBN>::B_STAGE);
+  cfg.dynamicSmemBytes = skinny_smem(p.a_region, p.stages, Skinny<kBN, kG>::B_STAGE);
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   int nattr = 0;
@@ -1447,10 +1459,10 @@ int launch_skinny(const Maps& m, const SkinnyParams& p, int grid, cudaStream_t s
   return cuda_check(cudaLaunchKernelEx(&cfg, kernel, m.a, m.w, m.out, m.a3, m.w3, m.wh, p), "fp8 skinny gemm launch");
 }
 
-template <int kBN, bool kQuantA>
+template <int kBN, bool kQuantA, int kG>
 int dispatch_skinny(int epilogue, bool tma, const Maps& m, const SkinnyParams& p, int grid, cudaStream_t s) {
 #define WBK_SK(E) \
-  return tma ? launch_skinny<kBN, E, true, kQuantA>(m, p, grid, s) : launch_skinny<kBN, E, false, kQuantA>(m, p, grid, s)
+  return tma ? launch_skinny<kBN, E, true, kQuantA, kG>(m, p, grid, s) : launch_skinny<kBN, E, false, kQuantA, kG>(m, p, grid, s)
   switch (epilogue) {
     case WBK_EPI_NONE: WBK_SK(WBK_EPI_NONE);
     case WBK_EPI_GELU: WBK_SK(WBK_EPI_GELU);
@@ -1739,7 +1751,10 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
     skinny = sp == 1;
   }
   const uint32_t sk_region = static_cast<uint32_t>(kblocks_all * kSkABlock + kSkASlack);
-  const int sk_bstage = bn == 64 ? Skinny<64>::B_STAGE : Skinny<128>::B_STAGE;
+  // 5 K blocks per weight stage when they divide K (64-wide tiles), else 2.
+  const bool sk_g5 = bn == 64 && kblocks_all % 5 == 0 && skinny_g5_enabled();
+  const int sk_g = sk_g5 ? 5 : 2;
+  const int sk_bstage = bn == 64 ? (sk_g5 ? Skinny<64, 5>::B_STAGE : Skinny<64>::B_STAGE) : Skinny<128>::B_STAGE;
   int sk_stages = 0;
   if (skinny) {
     const int64_t avail = 232448 - static_cast<int64_t>(skinny_smem(sk_region, 0, sk_bstage));
@@ -1751,7 +1766,7 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
   // (the skinny kernel: two K blocks per box for A and for each W stage).
   const int group = bn == 64 ? Tile<64>::G : (pair ? Tile<256, true>::G : Tile<128>::G);
   const int a_group = skinny ? 2 : group;  // the skinny kernel loads A two K blocks per box
-  const int w_group = skinny ? Skinny<64>::G : group;
+  const int w_group = skinny ? sk_g : group;
   bool grouped = K % BK == 0 && kblocks_grouping_enabled();
   if (grouped) {
     // If the driver does not take the blocked view, fall back to per-block 2-D loads.
@@ -1861,7 +1876,7 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
       if (halves <= grid) {
         const uint32_t half_rows = static_cast<uint32_t>(bn / 2);
         const int e = grouped ? make_tmap_kblocks(&maps.wh, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
-                                                  half_rows, static_cast<uint32_t>(Skinny<64>::G))
+                                                  half_rows, static_cast<uint32_t>(sk_g))
                               : make_tmap(&maps.wh, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, K, N, BK, half_rows,
                                           CU_TENSOR_MAP_SWIZZLE_128B);
         if (e != WBK_OK) return e;
@@ -1870,10 +1885,12 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
         sp.num_items = sp.num_tiles;
       }
     }
-    if (bn == 64) return qin ? dispatch_skinny<64, true>(epilogue, vec, maps, sp, grid, s)
-                             : dispatch_skinny<64, false>(epilogue, vec, maps, sp, grid, s);
-    return qin ? dispatch_skinny<128, true>(epilogue, vec, maps, sp, grid, s)
-               : dispatch_skinny<128, false>(epilogue, vec, maps, sp, grid, s);
+    if (bn == 64 && sk_g5) return qin ? dispatch_skinny<64, true, 5>(epilogue, vec, maps, sp, grid, s)
+                                      : dispatch_skinny<64, false, 5>(epilogue, vec, maps, sp, grid, s);
+    if (bn == 64) return qin ? dispatch_skinny<64, true, 2>(epilogue, vec, maps, sp, grid, s)
+                             : dispatch_skinny<64, false, 2>(epilogue, vec, maps, sp, grid, s);
+    return qin ? dispatch_skinny<128, true, 2>(epilogue, vec, maps, sp, grid, s)
+               : dispatch_skinny<128, false, 2>(epilogue, vec, maps, sp, grid, s);
   }
   if (qin != nullptr) return dispatch_epi<64, false, true>(epilogue, vec, maps, p, grid, s);
   if (bn == 64) return dispatch_epi<64>(epilogue, vec, maps, p, grid, s);
