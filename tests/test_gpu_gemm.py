@@ -283,6 +283,51 @@ def test_skinny_kernel_matches_general_kernel(cuda_device, tmp_path):
         assert torch.equal(y2.cpu().view(torch.int16), y2g.view(torch.int16)), (M, N, K, "gemm")
 
 
+# CTA-pair (256 x 256) residual epilogues load each 32 x 32 residual box by TMA into the store
+# staging buffer and write the output over it. Ragged M leaves boxes partly and wholly past row M
+# (zero fill, clipped store; at M = 4100 the second CTA of the last pair has no rows at all);
+# N % 32 == 8 leaves a partial last chunk; N % 8 != 0 takes the per-thread loads and direct stores.
+PAIR_RESIDUAL_SHAPES = [(4231, 2568, 384), (4100, 2560, 640), (4096, 2570, 384), (6000, 1280, 1280)]
+
+
+@pytest.mark.parametrize("epi,name", [(gemm.EPI_RESIDUAL, "residual"), (gemm.EPI_RESIDUAL_CLAMP, "residual_clamp")])
+@pytest.mark.parametrize("M,N,K", PAIR_RESIDUAL_SHAPES)
+def test_gemm_pair_residual_edges(cuda_device, epi, name, M, N, K):
+    aq, sa, wq, sw, b = _operands(M, N, K, 41 + N, cuda_device)
+    res = randn_f16((M, N), 43).to(cuda_device)
+    if epi == gemm.EPI_RESIDUAL_CLAMP:
+        res[-1, -4:] = torch.tensor([65504.0, -65504.0, 64000.0, 1.0], dtype=torch.float16)
+    out = torch.full((M + 1, N), float("nan"), dtype=torch.float16, device=cuda_device)  # one guard row
+    y = ops.gemm_fp8(aq, sa, wq, sw, b, res, name, out=out[:M])
+    _check(y, _ref(aq, sa, wq, sw, b, res, epi))
+    assert torch.isnan(out[M]).all()  # nothing stored past row M
+
+
+def test_pair_residual_tma_matches_thread_loads(cuda_device, tmp_path):
+    """The TMA-loaded residual gives bit-identical outputs to the per-thread residual
+    loads (WBK_GEMM_RES_TMA=0, run in a subprocess), ragged edges included."""
+    import os
+    import subprocess
+    import sys
+    cases = [(M, N, K, epi) for (M, N, K) in PAIR_RESIDUAL_SHAPES for epi in ("residual", "residual_clamp")]
+    path = str(tmp_path / "thread_loads.pt")
+    script = _GENERAL_KERNEL_SCRIPT.format(tests=os.path.dirname(os.path.abspath(__file__)), cases=cases, path=path)
+    env = dict(os.environ, WBK_GEMM_RES_TMA="0")
+    subprocess.run([sys.executable, "-c", script], env=env, check=True, timeout=600)
+    other = torch.load(path)
+    for (M, N, K, epi), (yg, qg, sg, y2g) in zip(cases, other):
+        x = randn_f16((M, K), M + K).to(cuda_device)
+        w = randn_f16((N, K), N, std=0.02).to(cuda_device)
+        b = randn_f16((N,), 5, std=0.02).to(cuda_device)
+        res = randn_f16((M, N), 6).to(cuda_device)
+        wq, sw = ops.quantise(w)
+        y, q, s = ops.linear_fp8(x, wq, sw, b, res, epi)
+        y2 = ops.gemm_fp8(q, s, wq, sw, b, res, epi)
+        assert torch.equal(q.cpu(), qg) and torch.equal(s.cpu(), sg), (M, N, K)
+        assert torch.equal(y.cpu().view(torch.int16), yg.view(torch.int16)), (M, N, K, epi, "linear")
+        assert torch.equal(y2.cpu().view(torch.int16), y2g.view(torch.int16)), (M, N, K, epi, "gemm")
+
+
 @pytest.mark.parametrize("M,N,K", [(1500, 5120, 1280), (64, 1280, 1280), (300, 1000, 1296)])
 def test_gemm_vs_reference_gpu_linear_path(cuda_device, M, N, K):
     """Against the reference's own GPU path for an FP8 linear (BlazeLinear.forward,

@@ -90,6 +90,7 @@ enum : uint32_t {
   SITE_EPI_ACC_FULL = 4,
   SITE_DRAIN = 5,
   SITE_QUANT_SYNC = 6,
+  SITE_EPI_RES = 7,
   SITE_SELFTEST = 15,
 };
 
@@ -110,6 +111,7 @@ struct SharedStorage {
   uint64_t empty[Tile<kBN, kPair>::STAGES];
   uint64_t acc_full[NUM_ACC];
   uint64_t acc_empty[NUM_ACC];
+  uint64_t res_full[EPI_WARPS][2];  // residual box landed in out[warp][buffer] (TMA residual path)
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -322,9 +324,12 @@ __device__ __forceinline__ void prefetch_residual(const Params& p, int row, int 
 // values in fp32 (descale, bias, activation, residual, clamp). Columns >= N
 // and rows >= M are never read from global memory.
 // bias_pre: the chunk's 32 bias values already loaded into registers (nullptr: load them).
+// res_all: `res` holds the whole chunk (a TMA box, zero past row M and column N)
+// even when the chunk is partial.
 template <int kEpi, bool kVec>
 __device__ __forceinline__ void epi_values(const Params& p, const uint32_t* acc, const uint4* res, int row, int col0,
-                                           float descale, float* v, const uint4* bias_pre = nullptr) {
+                                           float descale, float* v, const uint4* bias_pre = nullptr,
+                                           bool res_all = false) {
   const int N = p.N;
   const bool full = kVec && (col0 + 32 <= N);
   if (p.bias != nullptr && full) {
@@ -353,7 +358,7 @@ __device__ __forceinline__ void epi_values(const Params& p, const uint32_t* acc,
   for (int j = 0; j < 32; ++j) v[j] = epi_apply<kEpi>(v[j]);
   if (has_residual(kEpi)) {
     if (row < p.M) {
-      if (full) {
+      if (full || res_all) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) add_halves8(v + 8 * q, res[q]);
       } else {
@@ -403,11 +408,22 @@ __device__ __forceinline__ float absmax_valid(float m, const float* v, int valid
 
 // ------------------------------------------------------------------- kernel
 
-template <int kBN, int kEpi, bool kTmaStore, bool kPair, bool kQuantA>
+// The residual's tensor map, a kernel parameter only of the TMA-residual variants
+// (last in the parameter block, so the other kernels' parameters are unchanged).
+template <bool kOn>
+struct ResMap {
+  CUtensorMap map;
+};
+template <>
+struct ResMap<false> {};
+
+// kResTma: CTA-pair residual epilogues only; the residual arrives by TMA in the store staging buffers.
+template <int kBN, int kEpi, bool kTmaStore, bool kPair, bool kQuantA, bool kResTma = false>
 __global__ void __launch_bounds__(THREADS, 1)
 fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
                 const __grid_constant__ CUtensorMap tmap_out, const __grid_constant__ CUtensorMap tmap_a3,
-                const __grid_constant__ CUtensorMap tmap_w3, const KernelParams<kQuantA> p) {
+                const __grid_constant__ CUtensorMap tmap_w3, const KernelParams<kQuantA> p,
+                const __grid_constant__ ResMap<kResTma> res_map) {
   extern __shared__ uint8_t smem_raw[];
   SharedStorage<kBN, kPair>& s =
       *reinterpret_cast<SharedStorage<kBN, kPair>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -430,6 +446,10 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       mbar_init(&s.acc_full[i], 1);
       mbar_init(&s.acc_empty[i], kPair ? 2 * EPI_WARPS : EPI_WARPS);  // one arrival per epilogue warp (of the pair)
     }
+    for (int i = 0; i < EPI_WARPS; ++i) {
+      mbar_init(&s.res_full[i][0], 1);
+      mbar_init(&s.res_full[i][1], 1);
+    }
     mbar_init(&s.drain, 1);
     s.abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -441,6 +461,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       prefetch_tmap(&tmap_w);
     }
     if (kTmaStore) prefetch_tmap(&tmap_out);
+    if constexpr (kResTma) prefetch_tmap(&res_map.map);
   }
   if (warp == 1) {
     if (kPair) {
@@ -669,6 +690,26 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     int acc = 0;
     uint32_t acc_phase = 0;
     int sbuf = 0;  // staging buffer toggle (kTmaStore)
+    // CTA-pair residual epilogues (kResTma): each chunk's [32 rows x 32 columns]
+    // residual box is loaded by TMA, one chunk ahead, into the staging buffer its
+    // output is later stored from (same 64-byte swizzle), and the output overwrites
+    // it in place. One TMA load per 2 KB box replaces 128 per-thread 16-byte loads
+    // that each touch 32 rows.
+    static_assert(!kResTma || (kPair && kTmaStore && has_residual(kEpi)), "TMA residual: CTA-pair residual epilogues");
+    constexpr bool res_tma = kResTma;
+    uint32_t res_phase = 0u;    // parity of res_full[ew][b], bit b
+    uint32_t res_pending = 0u;  // buffers whose residual load has not been waited for
+    bool res_ok = true;
+    auto issue_res = [&](int b, int col0, int r0) {
+      if constexpr (kResTma) {
+        if (lane == 0) {
+          bulk_wait_read<0>();  // this warp's stores have finished reading their staging buffers
+          mbar_arrive_expect_tx(&s.res_full[ew][b], STAGE_OUT_BYTES);
+          tma_load_2d(&res_map.map, &s.res_full[ew][b], &s.out[ew][b][0], col0, r0);
+        }
+      }
+      res_pending |= 1u << b;
+    };
     prefetch_residual_l2<kBN, kEpi>(p, first_tile / p.splits, TL::ROWS, row_off, quarter, col_half, lane);
     for (int item = first_tile; item < p.num_items; item += tile_stride) {
       const int tile = item / p.splits;
@@ -679,7 +720,11 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       const int row0 = m0 + quarter * 32;
       const int row = row0 + lane;
       uint4 resa[4], resb[4];
-      prefetch_residual<kEpi, kTmaStore>(p, row, n0, resa);  // overlaps the tile's MMAs
+      if (res_tma) {
+        if (n0 < p.N) issue_res(sbuf, n0, row0);  // overlaps the tile's MMAs
+      } else {
+        prefetch_residual<kEpi, kTmaStore>(p, row, n0, resa);  // overlaps the tile's MMAs
+      }
       // 64-wide tiles (one 32-column chunk per warp): the bias is loaded before the
       // accumulator wait too, off the short-M GEMMs' critical path.
       uint4 bpre[4];
@@ -695,18 +740,36 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       const int nchunks = min(TL::EPI_COLS / CHUNK, (p.N - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
       auto process = [&](const uint32_t* regs, const uint4* res, int c) {
         const int col0 = n0 + c * CHUNK;
+        uint4 rs[4];
+        if constexpr (res_tma) {
+          const uint8_t* rbuf = &s.out[ew][0][0] + sbuf * STAGE_OUT_BYTES;
+          if (mbar_wait(&s.res_full[ew][sbuf], (res_phase >> sbuf) & 1u, abort_flag, p.timeout_ns, SITE_EPI_RES)) {
+            res_phase ^= 1u << sbuf;
+            res_pending &= ~(1u << sbuf);
+          } else {
+            res_ok = false;  // the tile loop ends after this tile
+          }
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            rs[q] = *reinterpret_cast<const uint4*>(rbuf + lane * 64 + (q ^ ((lane >> 1) & 3)) * 16);
+        }
         float v[32];
-        epi_values<kEpi, kTmaStore>(p, regs, res, row, col0, descale, v, (bias_early && c == 0) ? bpre : nullptr);
+        epi_values<kEpi, kTmaStore>(p, regs, res_tma ? rs : res, row, col0, descale, v,
+                                    (bias_early && c == 0) ? bpre : nullptr, res_tma);
         const int valid_cols = (row < p.M) ? min(CHUNK, p.N - col0) : 0;
         amax = kSignedMax ? max_valid(amax, v, valid_cols) : absmax_valid(amax, v, valid_cols);
         uint32_t w[16];
         pack_fp16(v, w);
         if (kTmaStore) {
           // Stage [32 rows x 64 B] with the 64-byte swizzle (16-byte chunk index
-          // XOR (row/2)%4), then one lane stores the box with TMA.
+          // XOR (row/2)%4), then one lane stores the box with TMA. With the TMA
+          // residual each lane overwrites only the 64 bytes it has just read, and
+          // the buffer was free before its residual load was issued.
           uint8_t* buf = &s.out[ew][0][0] + sbuf * STAGE_OUT_BYTES;
-          if (lane == 0) bulk_wait_read<1>();  // the store that last read `buf` is done
-          __syncwarp();
+          if (!res_tma) {
+            if (lane == 0) bulk_wait_read<1>();  // the store that last read `buf` is done
+            __syncwarp();
+          }
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
             const int chunk16 = q ^ ((lane >> 1) & 3);
@@ -819,21 +882,25 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
 #pragma unroll 1
       for (int c = 0; c < nchunks; c += 2) {
         const bool more1 = c + 1 < nchunks, more2 = c + 2 < nchunks;
+        // process() advances sbuf, so sbuf ^ 1 is always the buffer of the chunk after the current one.
         if (more1) {
           tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>((c + 1) * CHUNK), rb);
-          prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 1) * CHUNK, resb);
+          if (res_tma) issue_res(sbuf ^ 1, n0 + (c + 1) * CHUNK, row0);
+          else prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 1) * CHUNK, resb);
         }
         finish(ra, resa, c);
         if (more1) {
           tmem_ld_wait(rb);
           if (more2) {
             tmem_ld_32x32b_x32(taddr + static_cast<uint32_t>((c + 2) * CHUNK), ra);
-            prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 2) * CHUNK, resa);
+            if (res_tma) issue_res(sbuf ^ 1, n0 + (c + 2) * CHUNK, row0);
+            else prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 2) * CHUNK, resa);
           }
           finish(rb, resb, c + 1);
           if (more2) tmem_ld_wait(ra);
         }
       }
+      if (!res_ok) break;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -844,6 +911,14 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         acc = 0;
         acc_phase ^= 1u;
       }
+    }
+    // Abort path: a residual load that was never waited for may still be writing
+    // shared memory; wait for it (bounded) before the CTA can exit.
+    if (res_tma && res_pending != 0u) {
+      int no_abort = 0;
+      for (int b = 0; b < 2; ++b)
+        if (res_pending & (1u << b))
+          mbar_wait(&s.res_full[ew][b], (res_phase >> b) & 1u, &no_abort, 1000000ull, SITE_DRAIN);
     }
     // The staging buffers must have been read before the CTA exits; the global
     // writes themselves complete with the grid.
@@ -1308,16 +1383,16 @@ bool pdl_coop_enabled() {
   return on;
 }
 
-template <int kBN, int kEpi, bool kTma, bool kPair, bool kQuantA>
+template <int kBN, int kEpi, bool kTma, bool kPair, bool kQuantA, bool kResTma = false>
 int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap& to, const CUtensorMap& ta3,
-                const CUtensorMap& tw3, const QuantParams& qp, int grid, cudaStream_t stream) {
+                const CUtensorMap& tw3, const CUtensorMap& tr, const QuantParams& qp, int grid, cudaStream_t stream) {
   const KernelParams<kQuantA>& p = qp;
   static std::mutex mu;
   static std::vector<char> configured;
   const int dev = current_device();
   if (dev < 0) return fail(WBK_ERR_CUDA, "no current CUDA device");
   constexpr size_t kSmem = smem_bytes<kBN, kPair>();
-  auto kernel = fp8_gemm_kernel<kBN, kEpi, kTma, kPair, kQuantA>;
+  auto kernel = fp8_gemm_kernel<kBN, kEpi, kTma, kPair, kQuantA, kResTma>;
   {
     std::lock_guard<std::mutex> lock(mu);
     if (static_cast<int>(configured.size()) <= dev) configured.resize(dev + 1, 0);
@@ -1347,10 +1422,12 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
     attr[nattr].val.cooperative = 1;
     ++nattr;
   }
+  ResMap<kResTma> rm;
+  if constexpr (kResTma) rm.map = tr;
   if (!kPair) {
     cfg.attrs = attr;
     cfg.numAttrs = nattr;
-    return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, ta3, tw3, p), "fp8 gemm launch");
+    return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, ta3, tw3, p, rm), "fp8 gemm launch");
   }
   {
     // Persistent pairs: never launch more clusters than can be resident at once.
@@ -1384,13 +1461,25 @@ int launch_gemm(const CUtensorMap& ta, const CUtensorMap& tw, const CUtensorMap&
   ++nattr;
   cfg.attrs = attr;
   cfg.numAttrs = nattr;
-  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, ta3, tw3, p), "fp8 gemm (CTA pair) launch");
+  return cuda_check(cudaLaunchKernelEx(&cfg, kernel, ta, tw, to, ta3, tw3, p, rm), "fp8 gemm (CTA pair) launch");
 }
 
 struct Maps {
   CUtensorMap a, w, out, a3, w3;
-  CUtensorMap wh;  // skinny kernel: the weight box of a half-width item
+  CUtensorMap wh;   // skinny kernel: the weight box of a half-width item
+  CUtensorMap res;  // CTA-pair residual epilogues: the residual, boxed like `out`
+  bool res_tma = false;  // launch the TMA-residual variant (res is valid)
 };
+
+// TMA-loaded residual boxes in the CTA-pair residual epilogues (default on;
+// WBK_GEMM_RES_TMA=0 keeps per-thread residual loads).
+bool res_tma_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_GEMM_RES_TMA");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 // Five-K-block weight stages in the skinny kernel where they divide K (default on;
 // WBK_SKINNY_G=2 keeps two-block stages).
@@ -1475,8 +1564,12 @@ int dispatch_skinny(int epilogue, bool tma, const Maps& m, const SkinnyParams& p
 
 template <int kBN, int kEpi, bool kPair, bool kQuantA>
 int dispatch_store(bool tma, const Maps& m, const QuantParams& p, int grid, cudaStream_t s) {
-  return tma ? launch_gemm<kBN, kEpi, true, kPair, kQuantA>(m.a, m.w, m.out, m.a3, m.w3, p, grid, s)
-             : launch_gemm<kBN, kEpi, false, kPair, kQuantA>(m.a, m.w, m.out, m.a3, m.w3, p, grid, s);
+  if constexpr (kPair && has_residual(kEpi)) {
+    if (tma && m.res_tma)
+      return launch_gemm<kBN, kEpi, true, kPair, kQuantA, true>(m.a, m.w, m.out, m.a3, m.w3, m.res, p, grid, s);
+  }
+  return tma ? launch_gemm<kBN, kEpi, true, kPair, kQuantA>(m.a, m.w, m.out, m.a3, m.w3, m.res, p, grid, s)
+             : launch_gemm<kBN, kEpi, false, kPair, kQuantA>(m.a, m.w, m.out, m.a3, m.w3, m.res, p, grid, s);
 }
 
 template <int kBN, bool kPair = false, bool kQuantA = false>
@@ -1780,7 +1873,7 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
     maps.w3 = tw;
   }
 
-  QuantParams p;
+  QuantParams p{};  // zeroed: fields a path does not use stay 0
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -1852,6 +1945,15 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
   p.timeout_ns = wait_timeout_ns();
 
   if (pair) {
+    // Residual epilogues with TMA stores also load the residual by TMA (same box and swizzle).
+    if (needs_res && vec && res_tma_enabled()) {
+      if (int e = make_tmap(&maps.res, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, residual, N, M, CHUNK, 32,
+                            CU_TENSOR_MAP_SWIZZLE_64B))
+        return e;
+      maps.res_tma = true;
+    } else {
+      maps.res = to;  // unused
+    }
     const int pairs = sms / 2;
     const int grid = 2 * static_cast<int>(num_tiles < pairs ? num_tiles : pairs);
     return dispatch_epi<256, true>(epilogue, vec, maps, p, grid, s);
