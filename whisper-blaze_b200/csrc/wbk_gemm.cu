@@ -701,6 +701,9 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     uint32_t res_pending = 0u;  // buffers whose residual load has not been waited for
     bool res_ok = true;
     auto issue_res = [&](int b, int col0, int r0) {
+      // After a failed wait no further load is issued: a buffer may still have one in
+      // flight, and a second arrival on its barrier's pending phase is not allowed.
+      if (!res_ok) return;
       if constexpr (kResTma) {
         if (lane == 0) {
           bulk_wait_read<0>();  // this warp's stores have finished reading their staging buffers
@@ -743,11 +746,13 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         uint4 rs[4];
         if constexpr (res_tma) {
           const uint8_t* rbuf = &s.out[ew][0][0] + sbuf * STAGE_OUT_BYTES;
-          if (mbar_wait(&s.res_full[ew][sbuf], (res_phase >> sbuf) & 1u, abort_flag, p.timeout_ns, SITE_EPI_RES)) {
+          const bool landed =
+              res_ok && mbar_wait(&s.res_full[ew][sbuf], (res_phase >> sbuf) & 1u, abort_flag, p.timeout_ns, SITE_EPI_RES);
+          if (__all_sync(0xFFFFFFFFu, landed)) {  // warp-uniform phase and pending state
             res_phase ^= 1u << sbuf;
             res_pending &= ~(1u << sbuf);
           } else {
-            res_ok = false;  // the tile loop ends after this tile
+            res_ok = false;  // the tile loop ends after this tile; pending loads are drained at exit
           }
 #pragma unroll
           for (int q = 0; q < 4; ++q)
