@@ -221,6 +221,37 @@ def test_quantise_gelu_negative_side_amax(cuda_device):
     assert abs(s.item() * 448.0 - g.abs().max().item()) <= 2e-3 * g.abs().max().item()
 
 
+_GELU_FRESH_SCRIPT = r"""
+import sys, torch
+sys.path.insert(0, {tests!r})
+from conftest import randn_f16
+from whisper_blaze_b200 import ops
+dev = torch.device("cuda:0")
+y = randn_f16((1000, 5120), 301).to(dev)
+q1, s1 = ops.quantise_gelu(y, None)  # first launch in this process: the CTAs build the table
+q2, s2 = ops.quantise_gelu(y, None)  # CTA 0 of the first launch has published it by now
+torch.save((q1.cpu(), s1.cpu(), q2.cpu(), s2.cpu()), {path!r})
+"""
+
+
+def test_quantise_gelu_published_table(cuda_device, tmp_path):
+    """The GELU table is evaluated by the first launch on a device, which publishes it for the
+    CTAs that come later. The first launch in a fresh process and the next one give the same
+    codes and scale, equal to this process's result, and meet the oracle gate."""
+    import os
+    import subprocess
+    import sys
+    path = str(tmp_path / "gelu_fresh.pt")
+    script = _GELU_FRESH_SCRIPT.format(tests=os.path.dirname(os.path.abspath(__file__)), path=path)
+    subprocess.run([sys.executable, "-c", script], check=True, timeout=600)
+    q1, s1, q2, s2 = torch.load(path)
+    assert torch.equal(q1, q2) and torch.equal(s1, s2)
+    y = randn_f16((1000, 5120), 301)
+    q, s = ops.quantise_gelu(y.to(cuda_device), None)
+    assert torch.equal(q.cpu(), q1) and torch.equal(s.cpu(), s1)
+    _check_gelu_quant(y, q, s)
+
+
 @pytest.mark.parametrize("n", [1, 8, 4099, 8192, 81920, 81928, 262144, 262145])
 def test_small_tensor_path_matches_two_kernel_path(cuda_device, n):
     """wbk_quantise_f16 takes a single-CTA path up to 262144 elements (register-resident up to 81920,

@@ -214,6 +214,32 @@ __device__ __forceinline__ uint32_t gelu_q8x4(uint32_t h01, uint32_t h23, float 
 constexpr int kGeluThreads = 1024;
 constexpr size_t kGeluTableBytes = 65536 * sizeof(uint16_t);
 
+// The table never changes, so CTA 0 of the first launch that builds it also
+// publishes it here (one copy per device, 128 KB, held until the library is
+// unloaded); CTAs that find it published copy it from L2 instead of evaluating
+// erf 65536 times.
+__device__ __align__(16) uint16_t g_gelu_table[65536];
+__device__ uint32_t g_gelu_table_ready;
+
+// Fills the shared-memory table of this CTA (all threads call it).
+__device__ __forceinline__ void load_gelu_table(uint16_t* table) {
+  __shared__ uint32_t ready;
+  if (threadIdx.x == 0) asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(ready) : "l"(&g_gelu_table_ready) : "memory");
+  __syncthreads();
+  uint4* t4 = reinterpret_cast<uint4*>(table);
+  uint4* g4 = reinterpret_cast<uint4*>(g_gelu_table);
+  if (ready) {
+    for (int i = threadIdx.x; i < 65536 / 8; i += blockDim.x) t4[i] = __ldcg(g4 + i);
+    return;
+  }
+  for (uint32_t h = threadIdx.x; h < 65536u; h += blockDim.x) table[h] = static_cast<uint16_t>(gelu_f16_bits(h));
+  if (blockIdx.x != 0) return;
+  __syncthreads();
+  for (int i = threadIdx.x; i < 65536 / 8; i += blockDim.x) __stcg(g4 + i, t4[i]);
+  __syncthreads();
+  if (threadIdx.x == 0) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&g_gelu_table_ready), "r"(1u) : "memory");
+}
+
 __device__ __forceinline__ uint32_t gelu_lookup2(const uint16_t* table, uint32_t h2) {
   return static_cast<uint32_t>(table[h2 & 0xFFFFu]) | (static_cast<uint32_t>(table[h2 >> 16]) << 16);
 }
@@ -230,7 +256,7 @@ quantise_gelu_kernel(const __half* __restrict__ y, int64_t n, const uint32_t* __
                      float max_fp8, uint8_t* __restrict__ q, float* __restrict__ scale_out) {
   griddep_launch_dependents();  // a following GEMM may run its prologue meanwhile
   extern __shared__ uint16_t gelu_table[];
-  for (uint32_t h = threadIdx.x; h < 65536u; h += kGeluThreads) gelu_table[h] = static_cast<uint16_t>(gelu_f16_bits(h));
+  load_gelu_table(gelu_table);
   float scale, inv;
   scale_from_amax(*amax_bits, max_fp8, scale, inv);
   if (scale_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
