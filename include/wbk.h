@@ -60,6 +60,15 @@ const char* wbk_last_error(void);
  * current device. *code_out = 0 when no device-side error happened. */
 int wbk_device_error(uint32_t* code_out);
 
+/* Sets the wall-clock limit of every bounded device-side wait (GEMM, skinny
+ * GEMM, attention, in-kernel quantise arrivals) for launches made after this
+ * call, on every device; 0 restores the default (WBK_WAIT_TIMEOUT_MS, else
+ * 4 s). At most 60 s. A wait that runs out records WBK_ERR_DEVICE_TIMEOUT in
+ * the device error word and the kernel returns early, so a very short limit
+ * makes a launch give up: tests use it to run the kernels' abort paths.
+ * No reference counterpart (the reference's kernels have no bounded waits). */
+int wbk_set_wait_timeout_ns(uint64_t timeout_ns);
+
 /* Self-test of the bounded-wait machinery: launches one CTA that waits on an
  * mbarrier nothing ever arrives on, for at most `timeout_ns`, and records
  * WBK_ERR_DEVICE_TIMEOUT in the device error word. Used by tests to prove that

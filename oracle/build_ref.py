@@ -27,7 +27,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 NAME = "wbk_reference_kernels"
 SO_PATH = os.path.join(OUT_DIR, NAME + ".so")
-DEFAULT_REFERENCE = os.environ.get("WBK_REFERENCE_DIR", "/root/reference")
+# The reference tree: WBK_REFERENCE_DIR, else a `reference` directory beside this repository.
+DEFAULT_REFERENCE = os.environ.get("WBK_REFERENCE_DIR") or os.path.join(os.path.dirname(os.path.dirname(HERE)),
+                                                                         "reference")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -44,7 +44,13 @@ def test_noalloc_matches_existing_entry_point_on_consecutive_calls(cuda_device, 
     # second call must not inherit anything from the first call's scratch
     first = randn_f16((1500, 1280), 500) * 8
     second = randn_f16((4099,), 501, std=0.01)
-    for x in (first.to(cuda_device), second.to(cuda_device)):
+    # then a view one element into its buffer (not 16-byte aligned: the element-wise
+    # partial-max kernel and quantise path) spanning several CTAs, and an empty tensor
+    # (one CTA over an empty range: amax 0, scale 1)
+    shifted = randn_f16((200001,), 502, std=3.0).to(cuda_device)[1:]
+    assert shifted.data_ptr() % 16 != 0
+    empty = torch.empty(0, dtype=torch.float16, device=cuda_device)
+    for x in (first.to(cuda_device), second.to(cuda_device), shifted, empty):
         q_ref, s_ref = _quantise_reference(x, fmt)
         q, s = _quantise_noalloc(x, fmt)
         torch.cuda.synchronize()

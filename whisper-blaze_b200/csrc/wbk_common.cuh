@@ -27,6 +27,10 @@ int current_device();
 // Reads (and optionally clears) the device error word of the attention unit.
 int attn_read_device_error(uint32_t* v, bool clear);
 
+// Wall-clock limit of the bounded device waits set by wbk_set_wait_timeout_ns
+// (0 = not set: the WBK_WAIT_TIMEOUT_MS / 4 s default applies).
+uint64_t wait_timeout_override_ns();
+
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0;
 }

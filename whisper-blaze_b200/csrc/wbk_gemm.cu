@@ -597,16 +597,22 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         // Producer tail: wait until the MMA warp has released every stage, so
         // no tcgen05.commit arrival to this CTA's barriers is still in flight
         // when it exits.
-        for (int i = 0; i < TL::STAGES; ++i) {
-          if (!mbar_wait(&s.empty[stage], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) break;
-          if (++stage == TL::STAGES) {
-            stage = 0;
-            phase ^= 1u;
+        int st = stage;
+        uint32_t ph = phase;
+        for (int i = 0; i < TL::STAGES && ok; ++i) {
+          ok = mbar_wait(&s.empty[st], ph ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY);
+          if (++st == TL::STAGES) {
+            st = 0;
+            ph ^= 1u;
           }
         }
-      } else {
-        // Abort path: let the copies already issued land before the CTA exits.
-        // Stage i was last filled with phase (phase if i < stage else phase^1).
+      }
+      if (!ok) {
+        // Abort path (in the loop or in the tail): let the copies already issued
+        // land before the CTA exits. (stage, phase) is the ring position after the
+        // last fill, so stage i was last filled with parity phase if i < stage,
+        // else phase ^ 1 (a stage never filled then waits on the parity before
+        // its first phase, which reads as complete).
         for (int i = 0; i < TL::STAGES && (!kPair || rank == 0); ++i) {
           const uint32_t ph = (i < stage) ? phase : (phase ^ 1u);
           int dummy = 0;
@@ -1138,14 +1144,18 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
       }
       int dummy = 0;
       if (ok) {
-        for (int i = 0; i < stages; ++i) {  // every stage released: no commit arrival still in flight
-          if (!mbar_wait(&h.empty[st], phase ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY)) break;
-          if (++st == stages) {
-            st = 0;
-            phase ^= 1u;
+        int st2 = st;
+        uint32_t ph2 = phase;
+        for (int i = 0; i < stages && ok; ++i) {  // every stage released: no commit arrival still in flight
+          ok = mbar_wait(&h.empty[st2], ph2 ^ 1u, abort_flag, p.timeout_ns, SITE_PRODUCER_EMPTY);
+          if (++st2 == stages) {
+            st2 = 0;
+            ph2 ^= 1u;
           }
         }
-      } else {
+      }
+      if (!ok) {
+        // (st, phase) is the ring position after the last fill (the tail above did not move it)
         for (int i = 0; i < stages; ++i) {  // let the copies already issued land
           const uint32_t ph = (i < st) ? phase : (phase ^ 1u);
           mbar_wait(&h.full[i], ph, &dummy, 1000000ull, SITE_DRAIN);

@@ -1,4 +1,5 @@
 // Host-side error plumbing and device queries shared by every libwbk entry point.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -13,7 +14,10 @@ namespace wbk {
 
 namespace {
 thread_local std::string g_last_error;
+std::atomic<uint64_t> g_wait_timeout_ns{0};  // wbk_set_wait_timeout_ns; 0 = default
 }
+
+uint64_t wait_timeout_override_ns() { return g_wait_timeout_ns.load(std::memory_order_relaxed); }
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -58,5 +62,13 @@ extern "C" {
 int wbk_version(void) { return 1 * 10000 + 0 * 100 + 0; }
 
 const char* wbk_last_error(void) { return wbk::g_last_error.c_str(); }
+
+int wbk_set_wait_timeout_ns(uint64_t timeout_ns) {
+  if (timeout_ns > 60ull * 1000000000ull)
+    return wbk::fail(WBK_ERR_INVALID_ARG, "wbk_set_wait_timeout_ns: %llu ns is above the 60 s limit",
+                     static_cast<unsigned long long>(timeout_ns));
+  wbk::g_wait_timeout_ns.store(timeout_ns, std::memory_order_relaxed);
+  return WBK_OK;
+}
 
 }  // extern "C"

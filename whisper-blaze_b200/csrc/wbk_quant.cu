@@ -13,6 +13,7 @@
 // Layout in HBM: the input is a flat fp16 array (any shape, contiguous); the
 // output is a flat uint8 array of the same element count. Each thread moves
 // 8 elements per step: one 16-byte load in, one 8-byte store out.
+#include <cuda.h>
 #include <mutex>
 #include <vector>
 
@@ -534,24 +535,52 @@ amax_finalize_kernel(const uint32_t* __restrict__ partials, int count, uint32_t*
   }
 }
 
+// The current CUDA context (driver cuCtxGetCurrent, fetched once through the
+// runtime), or nullptr if none is current or the driver entry point is missing.
+void* current_context() {
+  using GetCtx = int (*)(void**);
+  static std::once_flag once;
+  static GetCtx fn = nullptr;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &f, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<GetCtx>(f);
+  });
+  void* ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
+
 // Device address of g_noalloc_scratch for the current device. The host-side
-// name is only a stand-in, so the address is looked up once per device (with
-// that device current) and cached.
+// name is only a stand-in, so the address is looked up (with that device
+// current) and cached per device together with the context it belongs to: a
+// new context on the device (after cudaDeviceReset, the module is loaded
+// again) makes the next call look the address up again.
 int noalloc_scratch(uint32_t** out) {
+  struct Entry {
+    void* ctx = nullptr;
+    uint32_t* ptr = nullptr;
+  };
   static std::mutex mu;
-  static std::vector<uint32_t*> cache;
+  static std::vector<Entry> cache;
   const int dev = current_device();
   if (dev < 0) return fail(WBK_ERR_CUDA, "wbk_quantise_f16_noalloc: no current CUDA device");
   std::lock_guard<std::mutex> lock(mu);
-  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1, nullptr);
-  if (cache[dev] == nullptr) {
+  if (static_cast<int>(cache.size()) <= dev) cache.resize(dev + 1);
+  Entry& e = cache[dev];
+  void* ctx = current_context();
+  if (e.ptr == nullptr || ctx == nullptr || ctx != e.ctx) {
     uint32_t* ptr = nullptr;
-    if (int e = cuda_check(cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch),
-                           "wbk_quantise_f16_noalloc: cudaGetSymbolAddress(scratch)"))
-      return e;
-    cache[dev] = ptr;
+    // also makes the device's primary context current if nothing had yet
+    if (int err = cuda_check(cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), g_noalloc_scratch),
+                             "wbk_quantise_f16_noalloc: cudaGetSymbolAddress(scratch)"))
+      return err;
+    e.ptr = ptr;
+    e.ctx = current_context();
   }
-  *out = cache[dev];
+  *out = e.ptr;
   return WBK_OK;
 }
 

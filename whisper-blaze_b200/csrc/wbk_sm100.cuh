@@ -306,14 +306,16 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// Host: wall-clock limit of every bounded device wait (WBK_WAIT_TIMEOUT_MS, default 4 s).
+// Host: wall-clock limit of every bounded device wait of a launch: the value set by
+// wbk_set_wait_timeout_ns if any, else WBK_WAIT_TIMEOUT_MS, else 4 s.
 uint64_t wait_timeout_ns() {
   static uint64_t t = [] {
     const char* e = std::getenv("WBK_WAIT_TIMEOUT_MS");
     const long long ms = e ? std::atoll(e) : 0;
     return static_cast<uint64_t>(ms > 0 ? ms : 4000) * 1000000ull;
   }();
-  return t;
+  const uint64_t o = wait_timeout_override_ns();
+  return o != 0 ? o : t;
 }
 
 }  // namespace

@@ -38,6 +38,7 @@ _PROTOTYPES = {
     "wbk_version": (_i32, []),
     "wbk_last_error": (ctypes.c_char_p, []),
     "wbk_device_error": (_i32, [_vp]),
+    "wbk_set_wait_timeout_ns": (_i32, [_u64]),
     "wbk_selftest_bounded_wait": (_i32, [_u64, _vp]),
     "wbk_amax_f16": (_i32, [_vp, _i64, _vp, _vp]),
     "wbk_quantise_from_amax_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
@@ -111,8 +112,33 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_TIMEOUT_HOOKS: list = []
+
+
+def on_device_timeout(fn):
+    """Register fn(device_index), run by device_error() when it reports a device-side
+    timeout on that device (e.g. to zero workspaces whose sync words a kernel that
+    gave up left behind). Usable as a decorator."""
+    _TIMEOUT_HOOKS.append(fn)
+    return fn
+
+
 def device_error() -> int:
-    """Read and clear the device-side error word of the current device (syncs)."""
+    """Read and clear the device-side error word of the current device (syncs).
+
+    The word is WBK_ERR_DEVICE_TIMEOUT | site << 8 after a bounded wait gave up.
+    A kernel that gave up may leave the sync words and split-K tickets of its
+    workspace non-zero, so on a timeout the registered hooks run first (the
+    library's own shared workspaces are zeroed again by ops)."""
     code = ctypes.c_uint32(0)
     check(lib().wbk_device_error(ctypes.byref(code)), "wbk_device_error")
+    if (code.value & 0xFF) == WBK_ERR_DEVICE_TIMEOUT:
+        dev = torch.cuda.current_device()
+        for fn in _TIMEOUT_HOOKS:
+            fn(dev)
     return code.value
+
+
+def set_wait_timeout_ns(timeout_ns: int) -> None:
+    """Limit of every bounded device wait for later launches (0 = the default)."""
+    check(lib().wbk_set_wait_timeout_ns(int(timeout_ns)), "wbk_set_wait_timeout_ns")

@@ -33,10 +33,13 @@ class BlazeLinear(nn.Module):
         if layer_prec.weight.is_fp8():
             self._quantise_weights()
 
-    def _quantise_weights(self) -> None:
+    def _quantise_weights(self, fmt: Optional[str] = None) -> None:
+        """Quantise the fp16 weight once (format `fmt`, default the weight precision's) and
+        keep its codes, device scale and fp16 bias on the weight's GPU (the current one if
+        the weight is on the host)."""
         dev = self.weight.device if self.weight.is_cuda else torch.device("cuda")
         w16 = self.weight.detach().to(dev, torch.float16).contiguous()
-        self._w_fp8, self._w_scale = ops.quantise(w16, self.layer_prec.weight.fmt())
+        self._w_fp8, self._w_scale = ops.quantise(w16, fmt or self.layer_prec.weight.fmt())
         if self._has_bias:
             self._bias16 = self.bias.detach().to(dev, torch.float16).contiguous()
 
@@ -47,17 +50,11 @@ class BlazeLinear(nn.Module):
         afmt = act.fmt() if act.is_fp8() else "e4m3"
         wfmt = self.layer_prec.weight.fmt() if self.layer_prec.weight.is_fp8() else "e4m3"
         if self._w_fp8 is None:
-            self._quantise_weights_as(wfmt)
+            self._quantise_weights(wfmt)
         # quantise(x) then the scaled GEMM; one kernel for short M (decoder steps)
         out, _, _ = ops.linear_fp8(x.half().contiguous(), self._w_fp8, self._w_scale, self._bias16, a_format=afmt,
                                    w_format=wfmt)
         return out
-
-    def _quantise_weights_as(self, fmt: str) -> None:
-        w16 = self.weight.detach().to("cuda", torch.float16).contiguous()
-        self._w_fp8, self._w_scale = ops.quantise(w16, fmt)
-        if self._has_bias:
-            self._bias16 = self.bias.detach().to(w16.device, torch.float16).contiguous()
 
 
 class StackedKVProjection(nn.Module):

@@ -266,6 +266,16 @@ def _scale_arg(scale: Scale, name: str, device) -> tuple[float, Optional[int]]:
 _SPLITK_WS: dict = {}
 
 
+@_lib.on_device_timeout
+def _zero_shared_workspaces(device_index: int) -> None:
+    """After a device-side timeout a kernel may have left the sync words or split-K tickets of
+    the device's shared workspace non-zero; zero it again so the next call starts clean.
+    (Workspaces passed by the caller are the caller's to zero, as wbk.h states.)"""
+    ws = _SPLITK_WS.get(torch.device("cuda", device_index))
+    if ws is not None:
+        ws.zero_()
+
+
 def splitk_workspace(device, nbytes: int) -> Optional[torch.Tensor]:
     """The per-device split-K workspace (zero-filled once, grown on demand).
 

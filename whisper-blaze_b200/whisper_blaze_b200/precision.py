@@ -75,15 +75,15 @@ def fp8_e4m3() -> PrecisionConfig:
 
 def mixed_fp8() -> PrecisionConfig:
     """Deprecated alias for :func:`full_fp16` (kept as in the reference)."""
-    warnings.warn("mixed_fp8() is deprecated and returns the FP16 configuration; "
-                  "FP8 execution is not available. Use full_fp16().", DeprecationWarning, stacklevel=2)
+    warnings.warn("mixed_fp8() is deprecated: it returns the all-FP16 configuration. Use full_fp16(), "
+                  "or fp8_e4m3() for FP8 linears.", DeprecationWarning, stacklevel=2)
     return full_fp16()
 
 
 def aggressive_fp8() -> PrecisionConfig:
     """Deprecated alias for :func:`full_fp16` (kept as in the reference)."""
-    warnings.warn("aggressive_fp8() is deprecated and returns the FP16 configuration; "
-                  "FP8 execution is not available. Use full_fp16().", DeprecationWarning, stacklevel=2)
+    warnings.warn("aggressive_fp8() is deprecated: it returns the all-FP16 configuration. Use full_fp16(), "
+                  "or fp8_e4m3() for FP8 linears.", DeprecationWarning, stacklevel=2)
     return full_fp16()
 
 
