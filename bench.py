@@ -1,7 +1,7 @@
 """Benchmark of the B200 FP8 quantised-matmul path (whisper-blaze north star).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload stack|layer|fc1|decoder|crossattn|attention|norms]
+                    [--workload stack|layer|fc1|decoder|crossattn|attention|norms|fp8peak]
 
 Default workload (config 5 of the north star): a 32-layer Whisper-large-v3
 encoder stack (d_model 1280, 20 heads, FFN 5120, pre-LN, every linear FP8
@@ -26,7 +26,9 @@ on one chunk on all host cores.
 Secondary workloads print their own line with their
 own metric: fc1 (config 1), layer (config 2), decoder (config 3), crossattn
 (config 4); attention (the encoder self-attention kernel against torch SDPA)
-and norms (the norm ops' HBM bandwidth) cover the other kernels.
+and norms (the norm ops' HBM bandwidth) cover the other kernels; fp8peak
+prints the measured dense FP8 ceiling alone (also measured, and used as
+`roofline.peak`, in every stack run on rank 0).
 """
 from __future__ import annotations
 
@@ -69,6 +71,62 @@ def fp8_peak(sustained: bool) -> tuple[float, str]:
     key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
     return 2.0 * p[key], (f"2 x {key} of {p['source']} MEASURED_PEAKS.json "
                           f"(dense fp8 tensor rate is 2x dense bf16 on B200)")
+
+
+def measure_fp8_peak(dev, seconds: float = 1.0, n: int = 8192) -> dict:
+    """Dense FP8 tensor rate of this GPU, measured now the way MEASURED_PEAKS.json measures the
+    bf16 one (a library GEMM): cuBLASLt's FP8 E4M3 GEMM (torch._scaled_mm, per-tensor fp32
+    scales, bf16 out) on n x n x n operands -- best of 10 calls (burst) and back to back for
+    `seconds` (sustained, under the power cap, SM clock sampled meanwhile). Our FP8 GEMM runs
+    the same shape the same two ways, for comparison. TFLOP/s = 2 n^3 / t."""
+    from whisper_blaze_b200 import ops
+    g = torch.Generator(device=dev)
+    g.manual_seed(7)
+    a = torch.randn(n, n, generator=g, device=dev).to(torch.float8_e4m3fn)
+    b = torch.randn(n, n, generator=g, device=dev).to(torch.float8_e4m3fn)
+    one = torch.ones((), dtype=torch.float32, device=dev)
+    a8, b8 = a.view(torch.uint8), b.view(torch.uint8)
+    out16 = torch.empty(n, n, dtype=torch.float16, device=dev)
+    flops = 2.0 * n ** 3
+    stream = torch.cuda.current_stream(dev)
+
+    def lib_call():
+        return torch._scaled_mm(a, b.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16)
+
+    def our_call():
+        return ops.gemm_fp8(a8, one, b8, one, out=out16)
+
+    def rates(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        best = float("inf")
+        for _ in range(10):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            fn()
+            e.record(stream)
+            e.synchronize()
+            best = min(best, s.elapsed_time(e))
+        # sustained: enough back-to-back calls to fill `seconds` at the burst rate
+        calls = max(10, int(seconds * 1e3 / best))
+        with ClockSampler(dev.index) as clk:
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            for _ in range(calls):
+                fn()
+            e.record(stream)
+            e.synchronize()
+        c = clk.summary()
+        return flops / best / 1e9, flops * calls / s.elapsed_time(e) / 1e9, c.get("sm_mhz"), c.get("reasons")
+
+    lb, ls, lmhz, lreasons = rates(lib_call)
+    ob, os_, omhz, _ = rates(our_call)
+    return {"shape": f"{n}x{n}x{n} e4m3", "cublaslt_fp8_tflops_burst": lb, "cublaslt_fp8_tflops_sustained": ls,
+            "cublaslt_sustained_sm_mhz": lmhz, "cublaslt_sustained_reasons": lreasons,
+            "ours_tflops_burst": ob, "ours_tflops_sustained": os_, "ours_sustained_sm_mhz": omhz,
+            "method": "torch._scaled_mm (cuBLASLt) and ops.gemm_fp8 on the same operands; best of 10 calls "
+                      f"and {seconds:.1f} s back to back, CUDA events, NVML clocks"}
 
 
 class ClockSampler:
@@ -270,7 +328,8 @@ def run_reference_arm(args, world, rank):
 
 def run_stack(args, world, rank, local):
     from whisper_blaze_b200 import ops
-    from whisper_blaze_b200.encoder import EncoderConfig, FP8EncoderStack, LayerWeights
+    from whisper_blaze_b200.encoder import (EncoderConfig, FP8EncoderStack, synthetic_hidden,
+                                            synthetic_stack_weights)
     from whisper_blaze_b200.sharding import gather_batch, shard_bounds
 
     dev = torch.device("cuda", local)
@@ -279,29 +338,13 @@ def run_stack(args, world, rank, local):
     D, Fd = cfg.d_model, cfg.ffn
 
     # random-init weights, generated on the device from a seeded generator (identical on every rank)
-    gen = torch.Generator(device=dev)
-    gen.manual_seed(1234)
-
-    def n(*shape):
-        return (torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32) * 0.02).half()
-
-    layers = []
-    for _ in range(cfg.layers):
-        b_qkv = n(3 * D)
-        b_qkv[D:2 * D] = 0
-        layers.append(LayerWeights(
-            ln1_g=torch.ones(D, dtype=torch.float16, device=dev), ln1_b=torch.zeros(D, dtype=torch.float16, device=dev),
-            w_qkv=n(3 * D, D), b_qkv=b_qkv, w_o=n(D, D), b_o=n(D),
-            ln2_g=torch.ones(D, dtype=torch.float16, device=dev), ln2_b=torch.zeros(D, dtype=torch.float16, device=dev),
-            w_fc1=n(Fd, D), b_fc1=n(Fd), w_fc2=n(D, Fd), b_fc2=n(D)))
+    layers = synthetic_stack_weights(cfg, dev, seed=1234)
     stack = FP8EncoderStack(cfg, layers, dev, slice_chunks=args.slice_chunks or None)
     del layers
 
     start, stop = shard_bounds(TOTAL_CHUNKS, world, rank)
     local_b = stop - start
-    gx = torch.Generator(device=dev)
-    gx.manual_seed(99 + rank)
-    x = torch.randn(local_b, cfg.seq_len, D, generator=gx, device=dev, dtype=torch.float32).half()
+    x = synthetic_hidden(local_b, cfg, dev, seed=99 + rank)
 
     def step():
         y = stack.forward_graphed(x) if args.graph else stack.forward(x)
@@ -390,6 +433,39 @@ def run_stack(args, world, rank, local):
     h2d = sum_over_ranks(float(x_host.numel() * 2), world, dev)
     d2h = TOTAL_CHUNKS * cfg.seq_len * D * 2
 
+    multi = None
+    if world > 1:
+        # The gather alone (device time, max over ranks), then a bitwise check on rank 0: each
+        # rank's slice of the gathered output equals this process's own forward of that rank's
+        # shard, regenerated from its seed. Activation scales are per rank's local batch.
+        y = stack.forward_graphed(x)
+        torch.cuda.synchronize()
+        barrier(world)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        full = gather_batch(y, TOTAL_CHUNKS)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        gather_ms = max_over_ranks(g0.elapsed_time(g1), world, dev)
+        check = None
+        if rank == 0:
+            bad = []
+            for r in range(world):
+                s, e = shard_bounds(TOTAL_CHUNKS, world, r)
+                yr = stack.forward(synthetic_hidden(e - s, cfg, dev, seed=99 + r))
+                if not torch.equal(full[s:e], yr):
+                    bad.append(r)
+            check = "bit-identical" if not bad else f"MISMATCH on ranks {bad}"
+        barrier(world)
+        multi = {"gather_ms": gather_ms, "gather_bytes": int(full.numel() * 2), "gather_check": check,
+                 "gather_check_how": "rank 0 recomputes every rank's shard (same seed) on its own GPU and "
+                                     "compares it with that rank's slice of the all_gather output, bit for bit",
+                 "scale_semantics": "per-tensor activation scales are taken over each rank's local batch "
+                                    "(the reference quantises each linear's input as one tensor), so an "
+                                    "N-GPU output differs from the 1-GPU one within FP8 rounding"}
+
+    fp8pk = measure_fp8_peak(dev) if rank == 0 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         from whisper_blaze_b200.encoder import EncoderConfig as _C
@@ -402,8 +478,14 @@ def run_stack(args, world, rank, local):
                          f"(oracle/encoder.py), fp32 SDPA"}
 
     if rank == 0:
-        peak, peak_src = fp8_peak(sustained=True)
+        bf16x2, bf16x2_src = fp8_peak(sustained=True)
+        peak = fp8pk["cublaslt_fp8_tflops_sustained"]
+        peak_src = ("measured in this run: cuBLASLt FP8 E4M3 GEMM (torch._scaled_mm) 8192^3 back to back for "
+                    "1 s under the power cap (the library-GEMM method of MEASURED_PEAKS.json's bf16 figure)")
         achieved = gemm_flops / (gemm_ms * 1e-3) / 1e12 if gemm_ms > 0 else None
+        stack_mhz = clock_info.get("sm_mhz")
+        pk_mhz = fp8pk.get("cublaslt_sustained_sm_mhz")
+        frac_clk = (achieved / stack_mhz) / (peak / pk_mhz) if achieved and stack_mhz and pk_mhz else None
         value = TOTAL_CHUNKS / (ms * 1e-3)
         line = {
             "metric": "encoder chunks/s (32-layer FP8 Whisper-large-v3 encoder stack)",
@@ -420,6 +502,12 @@ def run_stack(args, world, rank, local):
             "roofline": {"bound": "tensor", "kernel": "wbk fp8_gemm_kernel (tcgen05 kind::f8f6f4)",
                          "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                          "frac": (achieved / peak) if achieved else None, "peak_source": peak_src,
+                         "frac_clock_normalised": frac_clk,
+                         "frac_clock_normalised_how": "(achieved / the stack's median SM MHz) / (peak / the peak "
+                                                      "run's median SM MHz)",
+                         "fp8_peak_probe": fp8pk,
+                         "frac_of_2x_bf16_sustained": (achieved / bf16x2) if achieved else None,
+                         "bf16x2_source": bf16x2_src,
                          "frac_of_nominal_fp8_4500": (achieved / NOMINAL_FP8_TFLOPS) if achieved else None,
                          "gemm_launches_timed": n_gemm, "gemm_ms_per_step": gemm_ms / roofline_steps,
                          "gemm_share_of_step": (gemm_ms / roofline_steps) / ms_local,
@@ -432,6 +520,8 @@ def run_stack(args, world, rank, local):
             "clocks": clock_info,
             "cpu_baseline": cpu,
         }
+        if multi is not None:
+            line["multi_gpu"] = multi
         print(json.dumps(line), flush=True)
 
 
@@ -736,13 +826,29 @@ def run_norms(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
+def run_fp8peak(args, world, rank, local):
+    """The measured dense FP8 ceiling alone (measure_fp8_peak): cuBLASLt FP8 GEMM and ours on 8192^3."""
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if rank != 0:
+        return
+    pk = measure_fp8_peak(dev, seconds=max(1.0, float(args.steps) / 10))
+    v = pk["cublaslt_fp8_tflops_sustained"]
+    line = {"metric": "dense FP8 E4M3 GEMM TFLOP/s (library GEMM, sustained)", "value": v, "unit": "TFLOP/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "dtype": "fp8 e4m3",
+            "data": "synthetic", "config": {"workload": "fp8peak", "shape": pk["shape"]}, "probe": pk,
+            "frac_of_nominal_fp8_4500": v / NOMINAL_FP8_TFLOPS}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["stack", "layer", "fc1", "decoder", "crossattn", "attention", "norms"],
+    ap.add_argument("--workload", choices=["stack", "layer", "fc1", "decoder", "crossattn", "attention", "norms",
+                                           "fp8peak"],
                     default="stack")
     ap.add_argument("--chunks", type=int, default=64, help="batch of the attention workload")
     ap.add_argument("--shapes", default="", help="comma-separated shape names to keep (gemm workloads; for profiling)")
@@ -766,6 +872,8 @@ def main():
             run_attention(args, world, rank, local)
         elif args.workload == "norms":
             run_norms(args, world, rank, local)
+        elif args.workload == "fp8peak":
+            run_fp8peak(args, world, rank, local)
         else:
             run_gemm_configs(args, world, rank, local)
     finally:

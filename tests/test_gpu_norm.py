@@ -115,7 +115,9 @@ def test_layernorm_matches_live_reference_kernel(cuda_device):
     assert ((r.float() - r_ref.float()).abs() <= norm.ln_tolerance(r_ref.float().cpu()).to(cuda_device)).all()
 
 
-@pytest.mark.parametrize("rows,D", [(1, 8), (7, 64), (1500, 1280), (333, 1288), (64, 4096)])
+@pytest.mark.parametrize("rows,D", [(1, 8), (7, 64), (1500, 1280), (333, 1288), (64, 4096),
+                                    # many rows per warp: the row ring of both passes wraps several times
+                                    (20000, 1280), (5003, 2056), (3001, 4096)])
 @pytest.mark.parametrize("fmt", ["e4m3", "e5m2"])
 def test_layernorm_quantise_is_bit_identical_to_unfused(cuda_device, rows, D, fmt):
     """The fused LayerNorm->FP8 path writes exactly the codes and scale of LayerNorm then quantise."""

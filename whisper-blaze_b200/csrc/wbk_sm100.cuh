@@ -64,12 +64,33 @@ __device__ __forceinline__ void record_device_error(uint32_t code, uint32_t site
 // Bounded wait: true when the phase with `parity` completed; false when the
 // CTA abort flag is raised or `timeout_ns` of wall clock passed (the latter
 // records the error and raises the abort flag). Iterations are capped too.
+// Non-blocking probe of a phase (mbarrier.try_wait may suspend the thread for a
+// hardware time limit before it reports an incomplete phase).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Limits below this (set through wbk_set_wait_timeout_ns, for tests of the abort
+// paths) are enforced finely: the wait polls without suspending and reads the
+// clock every iteration, so it gives up as soon as the limit has passed. Longer
+// limits use the suspending try_wait and read the clock every 16 iterations.
+constexpr uint64_t kFineTimeoutNs = 1000000ull;
+
 __device__ __forceinline__ bool mbar_wait_loop(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                                uint64_t timeout_ns, uint32_t site) {
   const uint64_t t0 = globaltimer_ns();
+  const bool fine = timeout_ns < kFineTimeoutNs;
   for (uint32_t it = 0; it < (1u << 30); ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 15u) == 15u) {
+    if (fine ? mbar_test_wait(bar, parity) : mbar_try_wait(bar, parity)) return true;
+    if (fine || (it & 15u) == 15u) {
       if (*abort_flag) return false;
       if (globaltimer_ns() - t0 > timeout_ns) break;
     }

@@ -94,6 +94,40 @@ def random_layer_weights(cfg: EncoderConfig, gen: torch.Generator, std: float = 
         w_fc1=n(Fd, D), b_fc1=n(Fd), w_fc2=n(D, Fd), b_fc2=n(D))
 
 
+def synthetic_stack_weights(cfg: EncoderConfig, device, seed: int = 1234, std: float = 0.02) -> List[LayerWeights]:
+    """The benchmark's random-init weights: cfg.layers layers drawn in order on `device` from one
+    seeded generator (linears and biases ~ N(0, std), k bias 0, LN gamma 1 beta 0), so every
+    process that calls this with the same arguments holds the same bits."""
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    D, Fd = cfg.d_model, cfg.ffn
+
+    def n(*shape):
+        return (torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32) * std).half()
+
+    def const(v):
+        return torch.full((D,), v, dtype=torch.float16, device=dev)
+
+    layers = []
+    for _ in range(cfg.layers):
+        b_qkv = n(3 * D)
+        b_qkv[D:2 * D] = 0  # k_proj has no bias
+        layers.append(LayerWeights(ln1_g=const(1.0), ln1_b=const(0.0), w_qkv=n(3 * D, D), b_qkv=b_qkv,
+                                   w_o=n(D, D), b_o=n(D), ln2_g=const(1.0), ln2_b=const(0.0),
+                                   w_fc1=n(Fd, D), b_fc1=n(Fd), w_fc2=n(D, Fd), b_fc2=n(D)))
+    return layers
+
+
+def synthetic_hidden(chunks: int, cfg: EncoderConfig, device, seed: int) -> torch.Tensor:
+    """The benchmark's input shard: [chunks, seq_len, d_model] fp16 ~ N(0, 1), drawn on `device`
+    from a generator seeded with `seed` (the benchmark uses 99 + rank)."""
+    dev = torch.device(device)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(seed)
+    return torch.randn(chunks, cfg.seq_len, cfg.d_model, generator=gen, device=dev, dtype=torch.float32).half()
+
+
 @dataclass
 class _QuantLayer:
     ln1_g: torch.Tensor
@@ -259,13 +293,16 @@ class FP8EncoderStack:
 
     @torch.inference_mode()
     def forward(self, hidden: torch.Tensor, out: Optional[torch.Tensor] = None,
-                capture: Optional[List[dict]] = None) -> torch.Tensor:
+                capture: Optional[List[dict]] = None,
+                capture_layers: Optional[Sequence[int]] = None) -> torch.Tensor:
         """hidden [B, S, D] fp16 on this stack's device -> [B, S, D] fp16 (the final LayerNorm applied).
 
         capture: if a list is given, one dict per layer of copies of that
         layer's intermediates (LN outputs, fp8 codes and scales, qkv,
-        attention, fc1, residual sums) is appended — for stage-wise parity
-        checks; it costs copies, so it is off on the production path."""
+        attention, fc1, residual sums; "layer" holds the layer index) is
+        appended — for stage-wise parity checks; it costs copies, so it is off
+        on the production path. capture_layers restricts it to those layer
+        indices (the copies of one full-batch layer take about 4 GB)."""
         ops.require_input(hidden, "hidden")
         ops.require_fp16(hidden, "hidden")
         B, S, D = hidden.shape
@@ -290,8 +327,8 @@ class FP8EncoderStack:
                 for i, L in enumerate(self.layers):
                     nxt = bufs[i % 2]
                     cap = None
-                    if capture is not None:
-                        cap = {"in": h.clone()}
+                    if capture is not None and (capture_layers is None or i in capture_layers):
+                        cap = {"in": h.clone(), "layer": i}
                         capture.append(cap)
                     self._layer(L, h, nxt, nb, S, cap)
                     h = nxt
