@@ -328,6 +328,42 @@ def test_pair_residual_tma_matches_thread_loads(cuda_device, tmp_path):
         assert torch.equal(y2.cpu().view(torch.int16), y2g.view(torch.int16)), (M, N, K, epi, "gemm")
 
 
+# CTA pairs split the tiles of a partial last round into 2 or 4 narrower items (MMA N = 128 or
+# 64; 74 pairs on a B200). Run with WBK_GEMM_BN=256 so every shape takes the pair kernel:
+NARROW_CASES = [(11900, 1280, 1280, "residual"),      # 235 tiles = 3 rounds + 13 -> 52 quarter items; ragged M
+                (6300, 1288, 640, "residual_clamp"),  # 150 tiles = 2 rounds + 2 -> quarters; N 8 past a tile
+                (4100, 2560, 640, "none"),            # 170 tiles = 2 rounds + 22 -> 44 half items
+                (2000, 1000, 1280, "gelu"),           # 32 tiles, no whole round -> 64 halves; N % 32 = 8
+                (3000, 520, 256, "residual")]         # 36 tiles -> 72 halves
+
+
+def test_gemm_pair_narrow_last_round(cuda_device, tmp_path):
+    """Narrow last-round items meet the oracle gate and give bit-identical outputs to whole
+    tiles (WBK_GEMM_NARROW=0): the same K-ordered MMA accumulation per output element."""
+    import os
+    import subprocess
+    import sys
+    tests = os.path.dirname(os.path.abspath(__file__))
+    outs = {}
+    for tag, extra in (("narrow", {}), ("whole", {"WBK_GEMM_NARROW": "0"})):
+        path = str(tmp_path / f"{tag}.pt")
+        script = _GENERAL_KERNEL_SCRIPT.format(tests=tests, cases=NARROW_CASES, path=path)
+        env = dict(os.environ, WBK_GEMM_BN="256", **extra)
+        subprocess.run([sys.executable, "-c", script], env=env, check=True, timeout=600)
+        outs[tag] = torch.load(path)
+    epi_code = {"none": gemm.EPI_NONE, "gelu": gemm.EPI_GELU, "residual": gemm.EPI_RESIDUAL,
+                "residual_clamp": gemm.EPI_RESIDUAL_CLAMP}
+    for (M, N, K, epi), (y, q, s, y2), (yw, qw, sw_, y2w) in zip(NARROW_CASES, outs["narrow"], outs["whole"]):
+        w = randn_f16((N, K), N, std=0.02).to(cuda_device)
+        b = randn_f16((N,), 5, std=0.02)
+        res = randn_f16((M, N), 6) if epi.startswith("residual") else None
+        wq, sw = ops.quantise(w)
+        _check(y2, gemm.gemm_fp8_ref_f32(q, float(s.item()), wq.cpu(), float(sw.item()), b, res, epi_code[epi]))
+        assert torch.equal(q, qw) and torch.equal(s, sw_)
+        assert torch.equal(y2.view(torch.int16), y2w.view(torch.int16)), (M, N, K, epi)
+        assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
+
+
 @pytest.mark.parametrize("M,N,K", [(1500, 5120, 1280), (64, 1280, 1280), (300, 1000, 1296)])
 def test_gemm_vs_reference_gpu_linear_path(cuda_device, M, N, K):
     """Against the reference's own GPU path for an FP8 linear (BlazeLinear.forward,

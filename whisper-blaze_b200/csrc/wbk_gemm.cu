@@ -143,7 +143,29 @@ struct Params {
   int num_items;
   float* ws_partials;     // [num_items][128 rows][64 cols] fp32
   uint32_t* ws_tickets;   // [num_tiles][EPI_WARPS] arrival counts, zero between calls
+  // CTA pairs: items [0, full_items) are whole tiles; each tile past them is split
+  // into 2^narrow_shift column pieces (items of kBN >> narrow_shift columns, MMA N
+  // likewise), so a partial last round of whole tiles becomes a shorter round of
+  // narrow items. The narrow items' weight boxes come from the tensor map slot the
+  // kernel does not otherwise use (tmap_w when loads are grouped, else tmap_w3).
+  int full_items;
+  int narrow_shift;
 };
+
+// Pair item -> (tile, first column inside the tile, width in columns).
+template <int kBN>
+__device__ __forceinline__ void pair_item(const Params& p, int item, int& tile, int& col_off, int& width) {
+  if (item < p.full_items) {
+    tile = item;
+    col_off = 0;
+    width = kBN;
+    return;
+  }
+  const int j = item - p.full_items;
+  tile = p.full_items + (j >> p.narrow_shift);
+  width = kBN >> p.narrow_shift;
+  col_off = (j & ((1 << p.narrow_shift) - 1)) * width;
+}
 
 // Parameters of the in-kernel activation quantise (64-wide tiles, cooperative
 // launch): A is quantised per tensor from a_f16 into a_q, which the TMA then
@@ -384,8 +406,24 @@ __device__ __forceinline__ void pack_fp16(const float* v, uint32_t* w) {
   }
 }
 
+// max (of |v| with kAbs) over a full 32-column chunk as a depth-5 tree of fmaxf instead of a
+// 32-long dependent chain; fmaxf ignores NaN and is associative on everything else, so the
+// result equals the sequential maximum.
+template <bool kAbs>
+__device__ __forceinline__ float tree_max32(const float* v) {
+  float t[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) t[j] = kAbs ? fmaxf(fabsf(v[2 * j]), fabsf(v[2 * j + 1])) : fmaxf(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+  for (int w = 8; w >= 1; w >>= 1)
+#pragma unroll
+    for (int j = 0; j < w; ++j) t[j] = fmaxf(t[2 * j], t[2 * j + 1]);
+  return t[0];
+}
+
 // Running (signed) max of v over the valid columns (fmaxf ignores NaN).
 __device__ __forceinline__ float max_valid(float m, const float* v, int valid_cols) {
+  if (valid_cols >= 32) return fmaxf(m, tree_max32<false>(v));
 #pragma unroll
   for (int j = 0; j < 32; ++j)
     if (j < valid_cols) m = fmaxf(m, v[j]);
@@ -395,14 +433,10 @@ __device__ __forceinline__ float max_valid(float m, const float* v, int valid_co
 // Running max of |v| over the valid columns (fmaxf ignores NaN). Rounding to
 // fp16 is monotone and symmetric, so fp16(max |v|) is max |fp16(v)|.
 __device__ __forceinline__ float absmax_valid(float m, const float* v, int valid_cols) {
-  if (valid_cols >= 32) {
+  if (valid_cols >= 32) return fmaxf(m, tree_max32<true>(v));
 #pragma unroll
-    for (int j = 0; j < 32; ++j) m = fmaxf(m, fabsf(v[j]));
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < valid_cols) m = fmaxf(m, fabsf(v[j]));
-  }
+  for (int j = 0; j < 32; ++j)
+    if (j < valid_cols) m = fmaxf(m, fabsf(v[j]));
   return m;
 }
 
@@ -547,11 +581,16 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       int n_st = 0;  // stages issued so far; the first `pre` have their W half in flight already
       if constexpr (kQuantA) fence_async_global();
       for (int item = first_tile; item < p.num_items && ok; item += tile_stride) {
-        const int tile = item / p.splits;
+        int tile, col_off = 0, width = kBN;
+        if constexpr (kPair) pair_item<kBN>(p, item, tile, col_off, width);
+        else tile = item / p.splits;
         int kb0, kb1;
         split_range(p, TL::G, item - tile * p.splits, kb0, kb1);
         const int m0 = (tile / p.tiles_n) * TL::ROWS + row_off;
-        const int n0 = (tile % p.tiles_n) * kBN + static_cast<int>(rank) * TL::B_ROWS;
+        // each CTA of a pair loads half of the item's weight rows
+        const int n0 = (tile % p.tiles_n) * kBN + col_off + static_cast<int>(rank) * (kPair ? width / 2 : kBN);
+        const uint32_t b_sub = kPair ? static_cast<uint32_t>(width / 2) * BK : static_cast<uint32_t>(TL::B_SUB_BYTES);
+        const bool narrow = kPair && width < kBN;
         for (int kb = kb0; kb < kb1; kb += TL::G) {
           if constexpr (kQuantA) {
             if (n_st++ < pre) {  // W issued ahead: only A is left
@@ -568,19 +607,19 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
             break;
           }
           // A stage always receives G whole boxes per operand (blocks past K read as zeros).
-          const uint32_t stage_bytes = TL::G * (p.a_box_bytes + TL::B_SUB_BYTES);
+          const uint32_t stage_bytes = TL::G * (p.a_box_bytes + b_sub);
           if (kPair) {
             // Both CTAs' loads complete on the leader's full barrier, which expects both halves.
             if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * stage_bytes);
             const uint32_t full_leader = mapa_shared(&s.full[stage], 0);
             if (p.grouped) {
               tma_load_3d_pair(&tmap_a3, full_leader, s.a[stage], 0, m0, kb);
-              tma_load_3d_pair(&tmap_w3, full_leader, s.b[stage], 0, n0, kb);
+              tma_load_3d_pair(narrow ? &tmap_w : &tmap_w3, full_leader, s.b[stage], 0, n0, kb);
             } else {
 #pragma unroll
               for (int g = 0; g < TL::G; ++g) {
                 tma_load_2d_pair(&tmap_a, full_leader, s.a[stage] + g * p.a_box_bytes, (kb + g) * BK, m0);
-                tma_load_2d_pair(&tmap_w, full_leader, s.b[stage] + g * TL::B_SUB_BYTES, (kb + g) * BK, n0);
+                tma_load_2d_pair(narrow ? &tmap_w3 : &tmap_w, full_leader, s.b[stage] + g * b_sub, (kb + g) * BK, n0);
               }
             }
           } else {
@@ -631,6 +670,15 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       for (int item = first_tile; item < p.num_items && ok; item += tile_stride) {
         int kb0, kb1;
         split_range(p, TL::G, item % p.splits, kb0, kb1);
+        // narrow pair items: MMA N = the item's width, its weight rows stacked per K block
+        uint32_t idesc = p.idesc;
+        uint32_t b_sub = TL::B_SUB_BYTES;
+        if constexpr (kPair) {
+          int tile, col_off, width;
+          pair_item<kBN>(p, item, tile, col_off, width);
+          idesc = (p.idesc & ~(0x3Fu << 17)) | (static_cast<uint32_t>(width >> 3) << 17);
+          b_sub = static_cast<uint32_t>(width / 2) * BK;
+        }
         if (!mbar_wait(&s.acc_empty[acc], acc_phase ^ 1u, abort_flag, p.timeout_ns, SITE_MMA_ACC_EMPTY)) {
           ok = false;
           break;
@@ -648,15 +696,15 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
             const int kb = kbs + g;
             if (kb >= kb1) break;
             const uint64_t adesc = make_sw128_desc(s.a[stage] + g * p.a_box_bytes);
-            const uint64_t bdesc = make_sw128_desc(s.b[stage] + g * TL::B_SUB_BYTES);
+            const uint64_t bdesc = make_sw128_desc(s.b[stage] + g * b_sub);
 #pragma unroll
             for (int k = 0; k < BK / UMMA_K; ++k) {
               // Advance the start address by k*32 bytes inside the 128-byte swizzle row.
               const uint64_t koff = static_cast<uint64_t>((k * UMMA_K) >> 4);
               if (kPair)
-                umma_f8f6f4_pair(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                umma_f8f6f4_pair(d_tmem, adesc + koff, bdesc + koff, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
               else
-                umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, p.idesc, (kb > kb0 || k > 0) ? 1u : 0u);
+                umma_f8f6f4(d_tmem, adesc + koff, bdesc + koff, idesc, (kb > kb0 || k > 0) ? 1u : 0u);
             }
           }
           // frees this smem stage (in both CTAs of a pair) once its MMAs retire
@@ -721,11 +769,19 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
     };
     prefetch_residual_l2<kBN, kEpi>(p, first_tile / p.splits, TL::ROWS, row_off, quarter, col_half, lane);
     for (int item = first_tile; item < p.num_items; item += tile_stride) {
-      const int tile = item / p.splits;
-      prefetch_residual_l2<kBN, kEpi>(p, (item + tile_stride) / p.splits, TL::ROWS, row_off, quarter, col_half,
-                                      lane);  // next tile
+      int tile, col_off = 0, epi_cols = TL::EPI_COLS;  // this warp's columns of the item
+      if constexpr (kPair) {
+        int width;
+        pair_item<kBN>(p, item, tile, col_off, width);
+        epi_cols = width / 2;
+      } else {
+        tile = item / p.splits;
+      }
+      if (!kPair || item + tile_stride < p.full_items)
+        prefetch_residual_l2<kBN, kEpi>(p, (item + tile_stride) / p.splits, TL::ROWS, row_off, quarter, col_half,
+                                        lane);  // next tile
       const int m0 = (tile / p.tiles_n) * TL::ROWS + row_off;
-      const int n0 = (tile % p.tiles_n) * kBN + col_half * TL::EPI_COLS;
+      const int n0 = (tile % p.tiles_n) * kBN + col_off + col_half * epi_cols;
       const int row0 = m0 + quarter * 32;
       const int row = row0 + lane;
       uint4 resa[4], resb[4];
@@ -745,9 +801,9 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
       if (!mbar_wait(&s.acc_full[acc], acc_phase, abort_flag, p.timeout_ns, SITE_EPI_ACC_FULL)) break;
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                             static_cast<uint32_t>(acc * kBN + col_half * TL::EPI_COLS);
-      const int nchunks = min(TL::EPI_COLS / CHUNK, (p.N - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
-      auto process = [&](const uint32_t* regs, const uint4* res, int c) {
+                             static_cast<uint32_t>(acc * kBN + col_half * epi_cols);
+      const int nchunks = min(epi_cols / CHUNK, (p.N - n0 + CHUNK - 1) / CHUNK);  // warp-uniform, may be <= 0
+      auto process = [&](const uint32_t* regs, const uint4* res, int c, const uint4* bias_reg) {
         const int col0 = n0 + c * CHUNK;
         uint4 rs[4];
         if constexpr (res_tma) {
@@ -766,9 +822,11 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         }
         float v[32];
         epi_values<kEpi, kTmaStore>(p, regs, res_tma ? rs : res, row, col0, descale, v,
-                                    (bias_early && c == 0) ? bpre : nullptr, res_tma);
+                                    bias_reg != nullptr ? bias_reg : ((bias_early && c == 0) ? bpre : nullptr),
+                                    res_tma);
         const int valid_cols = (row < p.M) ? min(CHUNK, p.N - col0) : 0;
-        amax = kSignedMax ? max_valid(amax, v, valid_cols) : absmax_valid(amax, v, valid_cols);
+        if (kSignedMax || p.out_amax != nullptr)  // the running max only when an amax is asked for
+          amax = kSignedMax ? max_valid(amax, v, valid_cols) : absmax_valid(amax, v, valid_cols);
         uint32_t w[16];
         pack_fp16(v, w);
         if (kTmaStore) {
@@ -873,15 +931,15 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
         }
         return true;
       };
-      auto finish = [&](const uint32_t* regs, const uint4* res, int c) {
+      auto finish = [&](const uint32_t* regs, const uint4* res, int c, const uint4* bias_reg) {
         if constexpr (kBN == 64 && !kPair) {  // split-K exists only for the 64-wide (short-M) tiles
           if (p.splits > 1) {
             uint32_t sum[32];
-            if (split_reduce(regs, c, sum)) process(sum, res, c);
+            if (split_reduce(regs, c, sum)) process(sum, res, c, nullptr);
             return;
           }
         }
-        process(regs, res, c);
+        process(regs, res, c, bias_reg);
       };
       // Double-buffered drain: the TMEM load and the residual loads of chunk c+1
       // are in flight while chunk c is processed.
@@ -899,7 +957,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
           if (res_tma) issue_res(sbuf ^ 1, n0 + (c + 1) * CHUNK, row0);
           else prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 1) * CHUNK, resb);
         }
-        finish(ra, resa, c);
+        finish(ra, resa, c, nullptr);
         if (more1) {
           tmem_ld_wait(rb);
           if (more2) {
@@ -907,7 +965,7 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constan
             if (res_tma) issue_res(sbuf ^ 1, n0 + (c + 2) * CHUNK, row0);
             else prefetch_residual<kEpi, kTmaStore>(p, row, n0 + (c + 2) * CHUNK, resa);
           }
-          finish(rb, resb, c + 1);
+          finish(rb, resb, c + 1, nullptr);
           if (more2) tmem_ld_wait(ra);
         }
       }
@@ -1258,7 +1316,8 @@ fp8_skinny_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_const
         float v[32];
         epi_values<kEpi, kTmaStore>(p, regs, res, row, col0, descale, v);
         const int valid_cols = (row < p.M) ? min(CHUNK, p.N - col0) : 0;
-        amax = kSignedMax ? max_valid(amax, v, valid_cols) : absmax_valid(amax, v, valid_cols);
+        if (kSignedMax || p.out_amax != nullptr)  // the running max only when an amax is asked for
+          amax = kSignedMax ? max_valid(amax, v, valid_cols) : absmax_valid(amax, v, valid_cols);
         uint32_t w[16];
         pack_fp16(v, w);
         if (kTmaStore) {
@@ -1627,6 +1686,15 @@ bool kblocks_grouping_enabled() {
   return on;
 }
 
+// Narrow items for a CTA-pair GEMM's partial last round (default on; WBK_GEMM_NARROW=0 keeps whole tiles).
+bool narrow_tail_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("WBK_GEMM_NARROW");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 bool pair_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("WBK_GEMM_PAIR");
@@ -1943,6 +2011,8 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
     p.a_e5m2 = qin->a_fmt == WBK_FMT_E5M2 ? 1 : 0;
   }
   p.num_items = p.num_tiles * p.splits;
+  p.full_items = p.num_items;  // CTA pairs may narrow their last round below
+  p.narrow_shift = 0;
   p.alpha = alpha;
   p.a_scale = a_scale;
   p.w_scale = w_scale;
@@ -1970,7 +2040,28 @@ int gemm_impl(const void* A, const void* W, int64_t M, int64_t N, int64_t K, int
       maps.res = to;  // unused
     }
     const int pairs = sms / 2;
-    const int grid = 2 * static_cast<int>(num_tiles < pairs ? num_tiles : pairs);
+    // Last round: when the tiles past the whole rounds would leave most pairs idle, split
+    // each of them into 2 or 4 narrower items (all in one round). A narrow item costs more
+    // than its share of a tile (its A rows are loaded whole), but the round ends sooner.
+    if (narrow_tail_enabled()) {
+      const int64_t full = (num_tiles / pairs) * pairs;
+      const int64_t left = num_tiles - full;
+      const int shift = left == 0 ? 0 : (4 * left <= pairs ? 2 : (2 * left <= pairs ? 1 : 0));
+      if (shift > 0) {
+        // weight boxes of a narrow item: (128 >> shift) rows per CTA, in the slot the kernel
+        // does not otherwise read (tmap_w with grouped loads, tmap_w3 without)
+        const uint32_t rows_n = w_box_rows >> shift;
+        const int e = grouped ? make_tmap_kblocks(&maps.w, W, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
+                                                  rows_n, static_cast<uint32_t>(group))
+                              : make_tmap(&maps.w3, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, W, K, N, BK, rows_n,
+                                          CU_TENSOR_MAP_SWIZZLE_128B);
+        if (e != WBK_OK) return e;
+        p.full_items = static_cast<int>(full);
+        p.narrow_shift = shift;
+        p.num_items = static_cast<int>(full + (left << shift));
+      }
+    }
+    const int grid = 2 * (p.num_items < pairs ? p.num_items : pairs);
     return dispatch_epi<256, true>(epilogue, vec, maps, p, grid, s);
   }
   const int grid = p.num_items < sms ? p.num_items : sms;
