@@ -166,6 +166,25 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = D >> 3;
   const float fD = static_cast<float>(D);
+  // The fused LayerNorm->FP8 passes are issue-bound; gamma and beta are the same for
+  // every row, so they are converted to fp32 once per CTA into shared memory instead
+  // of being reloaded and unpacked for each row (the same fp32 values, so the outputs
+  // do not change). Layout [gamma lo, gamma hi, beta lo, beta hi][vector]: a warp's
+  // 16-byte reads of consecutive vectors are conflict-free.
+  constexpr bool kGbShared = kMode != kModeNormal;
+  __shared__ float4 s_gb[kGbShared ? 4 : 1][kGbShared ? kVpl * 32 : 1];
+  if constexpr (kGbShared) {
+    for (int idx = threadIdx.x; idx < nvec; idx += kThreads) {
+      float g[8], b[8];
+      unpack8(__ldg(reinterpret_cast<const uint4*>(gamma) + idx), g);
+      unpack8(__ldg(reinterpret_cast<const uint4*>(beta) + idx), b);
+      s_gb[0][idx] = make_float4(g[0], g[1], g[2], g[3]);
+      s_gb[1][idx] = make_float4(g[4], g[5], g[6], g[7]);
+      s_gb[2][idx] = make_float4(b[0], b[1], b[2], b[3]);
+      s_gb[3][idx] = make_float4(b[4], b[5], b[6], b[7]);
+    }
+    __syncthreads();
+  }
   float amax_f = 0.0f;
   float qinv = 0.0f;
   constexpr float kMx = kFmt == WBK_FMT_E4M3 ? 448.0f : 57344.0f;
@@ -202,7 +221,16 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
       const int idx = lane + 32 * i;
       if (idx < nvec) {
         float o[8];
-        normalise8<kRms>(v[i], idx, gamma, beta, inv, o);
+        if constexpr (kGbShared) {
+          // fma(d * inv, gamma, beta): the expression normalise8 evaluates, on the staged values
+          const float4 g0 = s_gb[0][idx], g1 = s_gb[1][idx], b0 = s_gb[2][idx], b1 = s_gb[3][idx];
+          const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+          const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] = fmaf(v[i][j] * inv, g[j], bb[j]);
+        } else {
+          normalise8<kRms>(v[i], idx, gamma, beta, inv, o);
+        }
         if (kMode != kModeQuant && out_amax) amax_f = absmax8(o, amax_f);
         if (kMode == kModeNormal) reinterpret_cast<uint4*>(out + row * D)[idx] = pack8(o);
         if (kMode == kModeQuant) {
