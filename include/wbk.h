@@ -127,6 +127,26 @@ int wbk_quantise_f16(const void* x, int64_t n, int fmt, void* q_out,
 int wbk_quantise_f16_noalloc(const void* x, int64_t n, int fmt, void* q_out,
                              float* scale_out, wbk_stream_t stream);
 
+/* Same codes, scale and amax bits as wbk_quantise_f16 (bit for bit), with x
+ * read from HBM about once instead of twice: ONE cooperative launch (one CTA
+ * per SM) keeps the end of each CTA's slice on chip -- 224 KB in shared
+ * memory and 256 KB in tensor memory (TMEM) per SM -- and reads the rest of
+ * the slice with an L2 evict-last hint so that it is still in L2, agrees on the
+ * amax through one bounded grid-wide arrival, then quantises the on-chip part
+ * and re-reads the rest.
+ * sync_ws: WBK_QUANT_SYNC_BYTES of device memory (16-byte aligned), zero-filled
+ * before first use; every call that completes leaves it zeroed; not used by two
+ * calls at once. After a WBK_ERR_DEVICE_TIMEOUT it must be zero-filled again.
+ * amax_ws ends holding the amax bits, as in wbk_quantise_f16.
+ * When n < 2^22 or n > 100 x 2^20, n % 8 != 0, x is not 16-byte aligned, q_out not 8-byte
+ * aligned or sync_ws is NULL, this is wbk_quantise_f16 (same results).
+ * Replaces: quantise_to_e4m3 / quantise_to_e5m2, fp8_quantize.cu:222-257, for
+ * the large activations (e.g. the 48000 x 1280 cross-attention input). */
+#define WBK_QUANT_SYNC_BYTES 16
+int wbk_quantise_f16_resident(const void* x, int64_t n, int fmt, void* q_out,
+                              float* scale_out, uint32_t* amax_ws, uint32_t* sync_ws,
+                              wbk_stream_t stream);
+
 /* scale_inv[0] = scale, scale_inv[1] = 1/scale for an accumulated amax, by the
  * same rule (and the same compiled division) as wbk_quantise_from_amax_f16.
  * Used by fused producers that quantise their own output. */

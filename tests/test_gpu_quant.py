@@ -262,3 +262,83 @@ def test_small_tensor_path_matches_two_kernel_path(cuda_device, n):
     ops.amax_accumulate(x, ws)
     q2, s2 = ops.quantise_from_amax(x, ws)
     assert torch.equal(q, q2) and s.view(torch.int32).item() == s2.view(torch.int32).item()
+
+
+def _pair_path(x, fmt_name):
+    ws = ops.new_amax_ws(x.device)
+    ops.amax_accumulate(x, ws)
+    q, s = ops.quantise_from_amax(x, ws, fmt_name)
+    return q, s, ws
+
+
+# n from the resident path's lower bound (2^22; every CTA's slice fits in shared memory) past
+# the points where the slices outgrow shared memory (148 x 14336 vectors = 17.0M elements) and
+# then tensor memory too (148 x 30720 vectors = 36.4M elements) to the 48000 x 1280
+# cross-attention input, plus sizes that do not divide evenly among the CTAs.
+RESIDENT_SIZES = [1 << 22, (1 << 22) + 8, 16_973_824 + 8 * 1001, 30_000_008, 36_372_480 + 8 * 77, 48000 * 1280]
+
+
+@pytest.mark.parametrize("fmt_name", ["e4m3", "e5m2"])
+@pytest.mark.parametrize("n", RESIDENT_SIZES)
+def test_resident_quantise_matches_two_kernel_path(cuda_device, n, fmt_name):
+    """wbk_quantise_f16_resident (one cooperative launch, tail of each slice kept on chip)
+    gives the codes, scale and amax bits of the amax kernel + quantise kernel pair, and leaves
+    its sync words zeroed (checked by running it twice on the same words)."""
+    assert n >= ops.RESIDENT_QUANT_MIN
+    x = randn_f16((n,), 500 + n % 89, std=2.0).to(cuda_device)
+    # the largest magnitude in the last vector (kept on chip) on one run, in the first on another
+    sync = torch.zeros(4, dtype=torch.int32, device=cuda_device)
+    for pos in (n - 3, 5):
+        x[pos] = 3000.0 if pos > 5 else -3500.0
+        amax = ops.new_amax_ws(cuda_device)
+        q, s = ops.quantise(x, fmt_name, amax_ws=amax, sync_ws=sync)
+        q2, s2, ws2 = _pair_path(x, fmt_name)
+        assert torch.equal(sync, torch.zeros_like(sync)), "sync words not reset"
+        assert amax.item() == ws2.item()
+        assert s.view(torch.int32).item() == s2.view(torch.int32).item()
+        assert torch.equal(q, q2), f"{int((q != q2).sum())} bytes differ"
+
+
+@pytest.mark.parametrize("with_inf", [True, False], ids=["inf_amax", "finite_amax"])
+@pytest.mark.parametrize("n", [30_000_008, 48000 * 1280])
+def test_resident_quantise_specials_and_shared_workspace(cuda_device, n, with_inf):
+    """NaN / inf / signed zero anywhere in the slices (shared-memory and TMEM parts, re-read
+    front) follow the element rule, with an infinite amax (scale inf, inv 0) and with NaNs but a
+    finite amax; the default sync words (the device's shared workspace) work call after call."""
+    x = randn_f16((n,), 611, std=1.0).to(cuda_device)
+    specials = _special_values(4096, seed=9)
+    if not with_inf:
+        specials = torch.nan_to_num(specials, nan=float("nan"), posinf=0.0, neginf=0.0)
+    specials = specials.to(cuda_device)
+    for off in (0, n // 2 - 2048, n - 4096, 21_000_000, n // 3 + 8):
+        x[off:off + 4096] = specials
+    for _ in range(2):
+        q, s = ops.quantise(x)
+        q2, s2, _ = _pair_path(x, "e4m3")
+        assert s.view(torch.int32).item() == s2.view(torch.int32).item()
+        assert torch.equal(q, q2)
+    for lo in (0, n // 3, n - 8192):  # against the oracle's element rule, specials included
+        q_ref = fp8.quantise_with_scale(x[lo:lo + 8192].cpu().numpy(), np.float32(s.item()), fp8.E4M3)
+        assert np.array_equal(q[lo:lo + 8192].cpu().numpy(), q_ref)
+
+
+@pytest.mark.parametrize("case", ["misaligned_x", "ragged_n", "null_sync", "above_max"])
+def test_resident_quantise_falls_back(cuda_device, case):
+    """Inputs the resident kernel does not take (x not 16-byte aligned, n % 8 != 0, no sync
+    words, more elements than it pays off for) go through wbk_quantise_f16 with the same results."""
+    n = ops.RESIDENT_QUANT_MIN + (3 if case == "ragged_n" else 0)
+    if case == "above_max":
+        n = ops.RESIDENT_QUANT_MAX + 8
+    base = randn_f16((n + 8,), 733, std=2.0).to(cuda_device)
+    x = base[4:4 + n] if case == "misaligned_x" else base[:n]
+    q = torch.empty(n, dtype=torch.uint8, device=cuda_device)
+    s = torch.empty(1, dtype=torch.float32, device=cuda_device)
+    amax = ops.new_amax_ws(cuda_device)
+    sync = torch.zeros(4, dtype=torch.int32, device=cuda_device)
+    rc = _lib.lib().wbk_quantise_f16_resident(x.data_ptr(), n, fp8.E4M3, q.data_ptr(), s.data_ptr(),
+                                              amax.data_ptr(), 0 if case == "null_sync" else sync.data_ptr(),
+                                              torch.cuda.current_stream().cuda_stream)
+    assert rc == 0
+    q2, s2, ws2 = _pair_path(x, "e4m3")
+    assert amax.item() == ws2.item() and torch.equal(q, q2)
+    assert s.view(torch.int32).item() == s2.view(torch.int32).item()

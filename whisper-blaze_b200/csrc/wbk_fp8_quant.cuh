@@ -49,10 +49,69 @@ __device__ __forceinline__ uint32_t q8x4(uint32_t h01, uint32_t h23, float inv, 
   return q8x2<kFmt>(f01.x, f01.y, inv, mx) | (q8x2<kFmt>(f23.x, f23.y, inv, mx) << 16);
 }
 
-// max |x| over eight fp16 values (one 16-byte vector) as fp16 bits, NaN ignored.
-__device__ __forceinline__ uint32_t absmax8_bits(const uint4& v) {
-  const uint32_t m = __vmaxu2(__vmaxu2(abs2_nonan(v.x), abs2_nonan(v.y)), __vmaxu2(abs2_nonan(v.z), abs2_nonan(v.w)));
-  return max(m & 0xFFFFu, m >> 16);
+// Two fp32 products in one instruction (mul.rn.f32x2): each lane is rounded
+// exactly as the scalar a * b.
+__device__ __forceinline__ float2 mul2_rn(float2 a, float s) {
+  float2 r;
+  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %4};\n\t"
+      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(s));
+  return r;
 }
+
+// The codes of q8x4 for any finite inv > 0 (inv is 0 only when the amax is
+// infinite; callers take q8x4 then), in fewer instructions:
+//  * a NaN lane becomes -65504 first (max.f16x2 returns the operand that is not
+//    NaN). The amax is an fp16 value, so 65504 >= amax and 65504 * inv is at
+//    least max_fp8 up to the rounding of the scale: the saturating
+//    round-to-nearest conversion gives -max_fp8, as the clamp gave for NaN (the
+//    nearest other codes, 416 and 49152, are far away);
+//  * every other product converts as after the clamp to [-max_fp8, max_fp8],
+//    because .satfinite saturates to +-max_fp8 exactly where the clamp would
+//    (infinities included);
+//  * the two fp32 products of a pair are one mul.rn.f32x2.
+template <int kFmt>
+__device__ __forceinline__ uint32_t q8x4_fin(uint32_t h01, uint32_t h23, float inv) {
+  constexpr uint32_t kNegMax2 = 0xFBFFFBFFu;  // two fp16 -65504
+  uint32_t a, b;
+  asm("max.f16x2 %0, %1, %2;" : "=r"(a) : "r"(h01), "r"(kNegMax2));
+  asm("max.f16x2 %0, %1, %2;" : "=r"(b) : "r"(h23), "r"(kNegMax2));
+  const float2 f01 = mul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&a)), inv);
+  const float2 f23 = mul2_rn(__half22float2(*reinterpret_cast<const __half2*>(&b)), inv);
+  constexpr __nv_fp8_interpretation_t it = kFmt == WBK_FMT_E4M3 ? __NV_E4M3 : __NV_E5M2;
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(f01, __NV_SATFINITE, it)) |
+         (static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(f23, __NV_SATFINITE, it)) << 16);
+}
+
+// Eight fp16 values (one 16-byte vector) -> eight fp8 codes; kFin selects
+// q8x4_fin (valid for finite inv > 0) over q8x4.
+template <int kFmt, bool kFin>
+__device__ __forceinline__ uint2 q8x8(const uint4& v, float inv, float mx) {
+  if constexpr (kFin) return make_uint2(q8x4_fin<kFmt>(v.x, v.y, inv), q8x4_fin<kFmt>(v.z, v.w, inv));
+  else return make_uint2(q8x4<kFmt>(v.x, v.y, inv, mx), q8x4<kFmt>(v.z, v.w, inv, mx));
+}
+
+// Running max of |x| over two packed fp16 values, NaN ignored: max.f16x2
+// returns the operand that is not NaN, and an accumulator started at 0 never
+// holds a NaN. Both halves hold the fp16 bits of values >= 0, whose unsigned
+// order is their numeric order, so the lanes equal the unsigned max of
+// abs2_nonan's lanes.
+__device__ __forceinline__ uint32_t hmax_abs2(uint32_t acc, uint32_t w) {
+  uint32_t r;
+  asm("max.f16x2 %0, %1, %2;" : "=r"(r) : "r"(acc), "r"(w & 0x7FFF7FFFu));
+  return r;
+}
+
+// Running max of |x| over one 16-byte vector of fp16 into a packed accumulator.
+__device__ __forceinline__ uint32_t absmax8_acc(uint32_t acc, const uint4& v) {
+  return hmax_abs2(hmax_abs2(hmax_abs2(hmax_abs2(acc, v.x), v.y), v.z), v.w);
+}
+
+// The packed accumulator's two lanes -> one fp16 bit pattern.
+__device__ __forceinline__ uint32_t absmax_lanes(uint32_t acc) { return max(acc & 0xFFFFu, acc >> 16); }
+
+// max |x| over eight fp16 values (one 16-byte vector) as fp16 bits, NaN ignored.
+__device__ __forceinline__ uint32_t absmax8_bits(const uint4& v) { return absmax_lanes(absmax8_acc(0u, v)); }
 
 }  // namespace wbk

@@ -28,9 +28,8 @@ constexpr int kThreads = 256;
 
 // -------------------------------------------------------------------- amax
 
-// Grid-stride max(|x|) over n fp16 values, NaN ignored, packed-fp16 integer
-// max (|x| as an unsigned bit pattern orders like the value for non-NaN).
-// One atomicMax per CTA into *amax_bits.
+// Grid-stride max(|x|) over n fp16 values, NaN ignored, as a packed fp16 max
+// (hmax_abs2). One atomicMax per CTA into *amax_bits.
 template <bool kVec>
 __global__ void __launch_bounds__(kThreads)
 amax_f16_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ amax_bits) {
@@ -48,26 +47,15 @@ amax_f16_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ 
       const uint4 v1 = ld_stream16_hint(xv + i + stride, keep);
       const uint4 v2 = ld_stream16_hint(xv + i + 2 * stride, keep);
       const uint4 v3 = ld_stream16_hint(xv + i + 3 * stride, keep);
-      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v0.x), abs2_nonan(v0.y)),
-                               __vmaxu2(abs2_nonan(v0.z), abs2_nonan(v0.w))));
-      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v1.x), abs2_nonan(v1.y)),
-                               __vmaxu2(abs2_nonan(v1.z), abs2_nonan(v1.w))));
-      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v2.x), abs2_nonan(v2.y)),
-                               __vmaxu2(abs2_nonan(v2.z), abs2_nonan(v2.w))));
-      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v3.x), abs2_nonan(v3.y)),
-                               __vmaxu2(abs2_nonan(v3.z), abs2_nonan(v3.w))));
+      m = absmax8_acc(absmax8_acc(absmax8_acc(absmax8_acc(m, v0), v1), v2), v3);
     }
-    for (; i < nvec; i += stride) {
-      const uint4 v = ld_stream16_hint(xv + i, keep);
-      m = __vmaxu2(m, __vmaxu2(__vmaxu2(abs2_nonan(v.x), abs2_nonan(v.y)),
-                               __vmaxu2(abs2_nonan(v.z), abs2_nonan(v.w))));
-    }
+    for (; i < nvec; i += stride) m = absmax8_acc(m, ld_stream16_hint(xv + i, keep));
     done = nvec << 3;
   }
   const unsigned short* xs = reinterpret_cast<const unsigned short*>(x);
-  for (int64_t i = done + tid; i < n; i += stride) m = __vmaxu2(m, abs2_nonan(xs[i]));
+  for (int64_t i = done + tid; i < n; i += stride) m = hmax_abs2(m, xs[i]);
 
-  uint32_t mm = max(m & 0xFFFFu, m >> 16);
+  uint32_t mm = absmax_lanes(m);
   mm = warp_max_u32(mm);
   __shared__ uint32_t red[kThreads / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -81,6 +69,27 @@ amax_f16_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ 
 }
 
 // ---------------------------------------------------------------- quantise
+
+// Codes of the 16-byte vectors [0, nvec) in grid-stride rounds from the LAST to
+// the first: the amax pass that ran just before read the tensor front to back,
+// so its most recent lines -- the ones still in L2 -- are read first here. Only
+// the order changes. kFin: inv is finite and > 0 (q8x4_fin's condition).
+template <int kFmt, bool kFin>
+__device__ __forceinline__ void quantise_vectors_back(const uint4* __restrict__ xv, uint2* __restrict__ qv, int64_t nvec,
+                                                      int64_t tid, int64_t stride, float inv, float max_fp8) {
+  const int64_t rounds = (nvec + stride - 1) / stride;
+  const uint64_t drop = l2_policy_evict_first();  // last use of the input
+  int64_t r = rounds - 1;
+  for (; r >= 1; r -= 2) {  // rounds r and r - 1 (r - 1 < rounds - 1 is a full round)
+    const int64_t i0 = r * stride + tid, i1 = i0 - stride;
+    const bool has0 = i0 < nvec;
+    const uint4 v0 = has0 ? ld_stream16_hint(xv + i0, drop) : make_uint4(0u, 0u, 0u, 0u);
+    const uint4 v1 = ld_stream16_hint(xv + i1, drop);
+    if (has0) qv[i0] = q8x8<kFmt, kFin>(v0, inv, max_fp8);
+    qv[i1] = q8x8<kFmt, kFin>(v1, inv, max_fp8);
+  }
+  if (r == 0 && tid < nvec) qv[tid] = q8x8<kFmt, kFin>(ld_stream16_hint(xv + tid, drop), inv, max_fp8);
+}
 
 template <int kFmt, bool kVec>
 __global__ void __launch_bounds__(kThreads)
@@ -98,24 +107,8 @@ quantise_f16_kernel(const __half* __restrict__ x, int64_t n, const uint32_t* __r
     const int64_t nvec = n >> 3;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
     uint2* qv = reinterpret_cast<uint2*>(q);
-    // Grid-stride rounds from the LAST to the first: the amax pass that ran just
-    // before read the tensor front to back, so its most recent lines -- the ones
-    // still in L2 -- are read first here. Only the order changes.
-    const int64_t rounds = (nvec + stride - 1) / stride;
-    const uint64_t drop = l2_policy_evict_first();  // last use of the input
-    int64_t r = rounds - 1;
-    for (; r >= 1; r -= 2) {  // rounds r and r - 1 (r - 1 < rounds - 1 is a full round)
-      const int64_t i0 = r * stride + tid, i1 = i0 - stride;
-      const bool has0 = i0 < nvec;
-      const uint4 v0 = has0 ? ld_stream16_hint(xv + i0, drop) : make_uint4(0u, 0u, 0u, 0u);
-      const uint4 v1 = ld_stream16_hint(xv + i1, drop);
-      if (has0) qv[i0] = make_uint2(q8x4<kFmt>(v0.x, v0.y, inv, max_fp8), q8x4<kFmt>(v0.z, v0.w, inv, max_fp8));
-      qv[i1] = make_uint2(q8x4<kFmt>(v1.x, v1.y, inv, max_fp8), q8x4<kFmt>(v1.z, v1.w, inv, max_fp8));
-    }
-    if (r == 0 && tid < nvec) {
-      const uint4 v = ld_stream16_hint(xv + tid, drop);
-      qv[tid] = make_uint2(q8x4<kFmt>(v.x, v.y, inv, max_fp8), q8x4<kFmt>(v.z, v.w, inv, max_fp8));
-    }
+    if (inv != 0.0f) quantise_vectors_back<kFmt, true>(xv, qv, nvec, tid, stride, inv, max_fp8);
+    else quantise_vectors_back<kFmt, false>(xv, qv, nvec, tid, stride, inv, max_fp8);  // an infinite amax
     done = nvec << 3;
   }
   for (int64_t i = done + tid; i < n; i += stride) {
@@ -245,10 +238,31 @@ __device__ __forceinline__ uint32_t gelu_lookup2(const uint16_t* table, uint32_t
   return static_cast<uint32_t>(table[h2 & 0xFFFFu]) | (static_cast<uint32_t>(table[h2 >> 16]) << 16);
 }
 
-template <int kFmt>
+template <int kFmt, bool kFin>
 __device__ __forceinline__ uint2 gelu_q8x8(const uint16_t* table, const uint4& v, float inv, float mx) {
-  return make_uint2(q8x4<kFmt>(gelu_lookup2(table, v.x), gelu_lookup2(table, v.y), inv, mx),
-                    q8x4<kFmt>(gelu_lookup2(table, v.z), gelu_lookup2(table, v.w), inv, mx));
+  const uint4 g = make_uint4(gelu_lookup2(table, v.x), gelu_lookup2(table, v.y), gelu_lookup2(table, v.z),
+                             gelu_lookup2(table, v.w));
+  return q8x8<kFmt, kFin>(g, inv, mx);
+}
+
+// Codes of the 16-byte vectors [0, nvec) of y's GELU (grid-stride, four per
+// thread per step). kFin: inv is finite and > 0 (q8x4_fin's condition).
+template <int kFmt, bool kFin>
+__device__ __forceinline__ void gelu_quantise_vectors(const uint16_t* table, const uint4* __restrict__ yv,
+                                                      uint2* __restrict__ qv, int64_t nvec, int64_t tid,
+                                                      int64_t stride, float inv, float mx) {
+  int64_t i = tid;
+  for (; i + 3 * stride < nvec; i += 4 * stride) {
+    const uint4 v0 = ld_stream16(yv + i);
+    const uint4 v1 = ld_stream16(yv + i + stride);
+    const uint4 v2 = ld_stream16(yv + i + 2 * stride);
+    const uint4 v3 = ld_stream16(yv + i + 3 * stride);
+    qv[i] = gelu_q8x8<kFmt, kFin>(table, v0, inv, mx);
+    qv[i + stride] = gelu_q8x8<kFmt, kFin>(table, v1, inv, mx);
+    qv[i + 2 * stride] = gelu_q8x8<kFmt, kFin>(table, v2, inv, mx);
+    qv[i + 3 * stride] = gelu_q8x8<kFmt, kFin>(table, v3, inv, mx);
+  }
+  for (; i < nvec; i += stride) qv[i] = gelu_q8x8<kFmt, kFin>(table, ld_stream16(yv + i), inv, mx);
 }
 
 template <int kFmt, bool kVec>
@@ -269,18 +283,8 @@ quantise_gelu_kernel(const __half* __restrict__ y, int64_t n, const uint32_t* __
     const int64_t nvec = n >> 3;
     const uint4* yv = reinterpret_cast<const uint4*>(y);
     uint2* qv = reinterpret_cast<uint2*>(q);
-    int64_t i = tid;
-    for (; i + 3 * stride < nvec; i += 4 * stride) {
-      const uint4 v0 = ld_stream16(yv + i);
-      const uint4 v1 = ld_stream16(yv + i + stride);
-      const uint4 v2 = ld_stream16(yv + i + 2 * stride);
-      const uint4 v3 = ld_stream16(yv + i + 3 * stride);
-      qv[i] = gelu_q8x8<kFmt>(gelu_table, v0, inv, max_fp8);
-      qv[i + stride] = gelu_q8x8<kFmt>(gelu_table, v1, inv, max_fp8);
-      qv[i + 2 * stride] = gelu_q8x8<kFmt>(gelu_table, v2, inv, max_fp8);
-      qv[i + 3 * stride] = gelu_q8x8<kFmt>(gelu_table, v3, inv, max_fp8);
-    }
-    for (; i < nvec; i += stride) qv[i] = gelu_q8x8<kFmt>(gelu_table, ld_stream16(yv + i), inv, max_fp8);
+    if (inv != 0.0f) gelu_quantise_vectors<kFmt, true>(gelu_table, yv, qv, nvec, tid, stride, inv, max_fp8);
+    else gelu_quantise_vectors<kFmt, false>(gelu_table, yv, qv, nvec, tid, stride, inv, max_fp8);  // infinite amax
     done = nvec << 3;
   }
   const unsigned short* ys = reinterpret_cast<const unsigned short*>(y);

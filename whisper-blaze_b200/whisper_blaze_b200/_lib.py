@@ -44,6 +44,7 @@ _PROTOTYPES = {
     "wbk_quantise_from_amax_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "wbk_quantise_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp]),
     "wbk_quantise_f16_noalloc": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp]),
+    "wbk_quantise_f16_resident": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp, _vp]),
     "wbk_quantise_gelu_f16": (_i32, [_vp, _i64, _i32, _vp, _vp, _vp, _vp, _vp]),
     "wbk_scale_from_amax": (_i32, [_vp, _i32, _vp, _vp]),
     "wbk_layernorm_quantise_f16": (_i32, [_vp, _vp, _vp, _i64, _i64, _f32, _i32, _vp, _vp, _vp, _vp, _vp]),

@@ -106,21 +106,50 @@ def quantise_from_amax(x: torch.Tensor, amax_ws: torch.Tensor, fmt="e4m3", q_out
     return q, s
 
 
+# Tensors of RESIDENT_QUANT_MIN to RESIDENT_QUANT_MAX elements (a multiple of 8,
+# 16-byte aligned) are quantised by the one-launch resident kernel
+# (wbk_quantise_f16_resident); the library applies the same bounds.
+RESIDENT_QUANT_MIN = 1 << 22
+RESIDENT_QUANT_MAX = 100 << 20
+_RESIDENT_SYNC_OFFSET = 32  # bytes: words 8..11 of the device's shared workspace (the GEMM's use 0..3)
+
+
 def quantise(x: torch.Tensor, fmt="e4m3", q_out: Optional[torch.Tensor] = None,
              scale_out: Optional[torch.Tensor] = None,
-             amax_ws: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
-    """Per-tensor quantise; returns (codes uint8, device fp32 scale [1]). No host sync."""
+             amax_ws: Optional[torch.Tensor] = None,
+             sync_ws: Optional[torch.Tensor] = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-tensor quantise; returns (codes uint8, device fp32 scale [1]). No host sync.
+
+    Large tensors (RESIDENT_QUANT_MIN to RESIDENT_QUANT_MAX elements) take one cooperative
+    launch that reads x from HBM about once; its grid-wide arrival uses 16 bytes
+    of sync words, by default in the device's shared workspace, so such calls
+    must not run concurrently on different streams: pass `sync_ws` (a zeroed
+    device tensor of 16 bytes, left zeroed by each call) to give a stream its
+    own. Codes, scale and amax are the same on either path."""
     require_input(x, "x")
     require_fp16(x, "x")
     f = fmt_code(fmt)
     q = torch.empty(x.shape, dtype=torch.uint8, device=x.device) if q_out is None else q_out
     s = torch.empty(1, dtype=torch.float32, device=x.device) if scale_out is None else scale_out
     ws = torch.empty(1, dtype=torch.int32, device=x.device) if amax_ws is None else amax_ws
-    require_same_device(x, q, s, ws)
+    require_same_device(x, q, s, ws, sync_ws)
+    n = x.numel()
     with torch.cuda.device(x.device):
-        check(lib().wbk_quantise_f16(x.data_ptr(), x.numel(), f, q.data_ptr(), s.data_ptr(), ws.data_ptr(),
-                                     stream_of(x)), "quantise")
-    _count(2)
+        if (RESIDENT_QUANT_MIN <= n <= RESIDENT_QUANT_MAX and n % 8 == 0 and x.data_ptr() % 16 == 0
+                and q.data_ptr() % 8 == 0):
+            if sync_ws is None:
+                sync_ptr = splitk_workspace(x.device, 256).data_ptr() + _RESIDENT_SYNC_OFFSET
+            else:
+                if sync_ws.numel() * sync_ws.element_size() < 16 or sync_ws.data_ptr() % 16 != 0:
+                    raise ValueError("sync_ws must hold 16 bytes at a 16-byte aligned address")
+                sync_ptr = sync_ws.data_ptr()
+            check(lib().wbk_quantise_f16_resident(x.data_ptr(), n, f, q.data_ptr(), s.data_ptr(), ws.data_ptr(),
+                                                  sync_ptr, stream_of(x)), "quantise")
+            _count(1)
+        else:
+            check(lib().wbk_quantise_f16(x.data_ptr(), n, f, q.data_ptr(), s.data_ptr(), ws.data_ptr(),
+                                         stream_of(x)), "quantise")
+            _count(2)
     return q, s
 
 
