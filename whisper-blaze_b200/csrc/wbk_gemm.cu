@@ -1531,6 +1531,11 @@ quantise_resident_kernel(const uint4* __restrict__ x, int64_t nvec, float mx, ui
   const int64_t t0 = r0 - min(r0 - v0, static_cast<int64_t>(kResTmemVecs) * kResThreads);  // TMEM [t0, r0)
   const uint32_t smem_bytes = static_cast<uint32_t>((v1 - r0) * 16);
   const uint64_t keep = l2_policy_evict_last(), drop = l2_policy_evict_first();
+  // Under programmatic dependent launch: x may still be being written by the
+  // grid before, and q read by it; a dependent grid may launch now (its CTAs
+  // wait in griddepcontrol.wait until this grid has finished).
+  griddep_wait();
+  griddep_launch_dependents();
   if (tid == 0) {
     mbar_init(&bar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -2391,11 +2396,18 @@ int wbk_quantise_f16_resident(const void* x, int64_t n, int fmt, void* q_out, fl
   cfg.blockDim = dim3(kResThreads, 1, 1);
   cfg.dynamicSmemBytes = kResSmemBytes;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;  // the CTAs wait for one another: all must be resident at once
-  attr[0].val.cooperative = 1;
+  cudaLaunchAttribute attr[2];
+  int nattr = 0;
+  attr[nattr].id = cudaLaunchAttributeCooperative;  // the CTAs wait for one another: all must be resident at once
+  attr[nattr].val.cooperative = 1;
+  ++nattr;
+  if (pdl_coop_enabled()) {  // the kernel waits (griddep_wait) before touching memory
+    attr[nattr].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[nattr].val.programmaticStreamSerializationAllowed = 1;
+    ++nattr;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = nattr;
   const uint4* xv = static_cast<const uint4*>(x);
   uint2* qv = static_cast<uint2*>(q_out);
   const float mx = fmt == WBK_FMT_E4M3 ? 448.0f : 57344.0f;
