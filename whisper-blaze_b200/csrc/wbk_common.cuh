@@ -37,6 +37,33 @@ inline bool aligned(const void* p, size_t a) {
 
 // ---------------------------------------------------------------- device side
 
+// Packed fp32 pairs (sm_100 add / mul / fma .rn.f32x2, one instruction for two
+// lanes): each lane is rounded exactly as the scalar operation would round it.
+__device__ __forceinline__ float2 f2_add(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "add.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 f2_mul(float2 a, float2 b) {
+  float2 r;
+  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\t"
+      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return r;
+}
+__device__ __forceinline__ float2 f2_fma(float2 a, float2 b, float2 c) {
+  float2 r;
+  asm("{\n\t.reg .b64 a, b, c, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %5};\n\tmov.b64 c, {%6, %7};\n\t"
+      "fma.rn.f32x2 d, a, b, c;\n\tmov.b64 {%0, %1}, d;\n\t}"
+      : "=f"(r.x), "=f"(r.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return r;
+}
+
 // |x| of two packed fp16 values with NaN lanes forced to 0 (so a max over
 // them ignores NaN, like fmaxf does). Infinity stays 0x7C00.
 __device__ __forceinline__ uint32_t abs2_nonan(uint32_t w) {

@@ -49,16 +49,8 @@ __device__ __forceinline__ uint32_t q8x4(uint32_t h01, uint32_t h23, float inv, 
   return q8x2<kFmt>(f01.x, f01.y, inv, mx) | (q8x2<kFmt>(f23.x, f23.y, inv, mx) << 16);
 }
 
-// Two fp32 products in one instruction (mul.rn.f32x2): each lane is rounded
-// exactly as the scalar a * b.
-__device__ __forceinline__ float2 mul2_rn(float2 a, float s) {
-  float2 r;
-  asm("{\n\t.reg .b64 a, b, d;\n\tmov.b64 a, {%2, %3};\n\tmov.b64 b, {%4, %4};\n\t"
-      "mul.rn.f32x2 d, a, b;\n\tmov.b64 {%0, %1}, d;\n\t}"
-      : "=f"(r.x), "=f"(r.y)
-      : "f"(a.x), "f"(a.y), "f"(s));
-  return r;
-}
+// Two fp32 products a.x * s, a.y * s in one instruction (f2_mul).
+__device__ __forceinline__ float2 mul2_rn(float2 a, float s) { return f2_mul(a, make_float2(s, s)); }
 
 // The codes of q8x4 for any finite inv > 0 (inv is 0 only when the amax is
 // infinite; callers take q8x4 then), in fewer instructions:

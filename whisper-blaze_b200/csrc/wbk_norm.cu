@@ -13,6 +13,7 @@
 // costs one atomic per CTA. Rows with D > 4096 use a CTA-per-row kernel that
 // re-reads the row (served from L2).
 #include "wbk_common.cuh"
+#include "wbk_fp8_quant.cuh"
 
 namespace wbk {
 namespace {
@@ -108,10 +109,15 @@ __device__ __forceinline__ void row_stats(float (&v)[kVpl][8], int lane, int nve
   }
   mean = s / fD;
   float var = 0.0f;
+  const float2 neg_mean = make_float2(-mean, -mean);
 #pragma unroll
   for (int i = 0; i < kVpl; ++i) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[i][j] -= mean;
+    for (int j = 0; j < 8; j += 2) {  // v - mean, two lanes per instruction
+      const float2 d = f2_add(make_float2(v[i][j], v[i][j + 1]), neg_mean);
+      v[i][j] = d.x;
+      v[i][j + 1] = d.y;
+    }
     if (lane + 32 * i < nvec) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) var += v[i][j] * v[i][j];
@@ -208,10 +214,15 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
       const float2 st = stats[row];
       mean = st.x;
       inv = st.y;
+      const float2 neg_mean = make_float2(-mean, -mean);
 #pragma unroll
       for (int i = 0; i < kVpl; ++i)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] -= mean;
+        for (int j = 0; j < 8; j += 2) {  // v - mean, two lanes per instruction
+          const float2 d = f2_add(make_float2(v[i][j], v[i][j + 1]), neg_mean);
+          v[i][j] = d.x;
+          v[i][j + 1] = d.y;
+        }
     } else {
       row_stats<kVpl, kRms>(v, lane, nvec, fD, eps, mean, inv);
       if (kMode == kModeStats && lane == 0) stats[row] = make_float2(mean, inv);
@@ -222,20 +233,39 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
       if (idx < nvec) {
         float o[8];
         if constexpr (kGbShared) {
-          // fma(d * inv, gamma, beta): the expression normalise8 evaluates, on the staged values
+          // fma(d * inv, gamma, beta): the expression normalise8 evaluates, on the staged
+          // values, two lanes per instruction (each lane rounded as the scalar form)
           const float4 g0 = s_gb[0][idx], g1 = s_gb[1][idx], b0 = s_gb[2][idx], b1 = s_gb[3][idx];
-          const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
-          const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+          const float2 g[4] = {make_float2(g0.x, g0.y), make_float2(g0.z, g0.w), make_float2(g1.x, g1.y),
+                               make_float2(g1.z, g1.w)};
+          const float2 bb[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                                make_float2(b1.z, b1.w)};
+          const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
-          for (int j = 0; j < 8; ++j) o[j] = fmaf(v[i][j] * inv, g[j], bb[j]);
+          for (int t = 0; t < 4; ++t) {
+            const float2 r = f2_fma(f2_mul(make_float2(v[i][2 * t], v[i][2 * t + 1]), inv2), g[t], bb[t]);
+            o[2 * t] = r.x;
+            o[2 * t + 1] = r.y;
+          }
         } else {
           normalise8<kRms>(v[i], idx, gamma, beta, inv, o);
         }
         if (kMode != kModeQuant && out_amax) amax_f = absmax8(o, amax_f);
         if (kMode == kModeNormal) reinterpret_cast<uint4*>(out + row * D)[idx] = pack8(o);
-        if (kMode == kModeQuant) {
-          // fp8(fp16(o) * (1/scale)): fmaxf maps NaN to -max as the quantiser's
-          // clamp does; satfinite clamps everything else to +-max.
+        if (kMode == kModeQuant && qinv != 0.0f) {
+          // fp8(fp16(o) * (1/scale)) by q8x4_fin (qinv is finite and > 0 here), the
+          // quantiser's element rule on the fp16 outputs.
+          uint32_t h[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const __half2 hh = __floats2half2_rn(o[2 * t], o[2 * t + 1]);
+            h[t] = *reinterpret_cast<const uint32_t*>(&hh);
+          }
+          reinterpret_cast<uint2*>(q_out + row * D)[idx] =
+              make_uint2(q8x4_fin<kFmt>(h[0], h[1], qinv), q8x4_fin<kFmt>(h[2], h[3], qinv));
+        } else if (kMode == kModeQuant) {
+          // An infinite amax (qinv = 0): fp8(fp16(o) * (1/scale)) where fmaxf maps NaN
+          // to -max as the quantiser's clamp does; satfinite clamps everything else to +-max.
           uint32_t q[2];
 #pragma unroll
           for (int t = 0; t < 2; ++t) {
