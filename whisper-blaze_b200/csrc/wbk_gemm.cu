@@ -1484,6 +1484,7 @@ __device__ __forceinline__ void resident_phase2(const uint4* __restrict__ x, uin
 #pragma unroll
   for (int b = 0; b < kResTmemVecs / 8; ++b) {
     uint4 v[8];
+    __syncwarp();  // converged (after the predicated stores of the batch before) for the warp-collective loads
 #pragma unroll
     for (int u = 0; u < 4; ++u) tmem_ld_2v(tmem_thr + (b * 8 + 2 * u) * 4, v[2 * u], v[2 * u + 1]);
     tmem_ld_wait_8v(v);
