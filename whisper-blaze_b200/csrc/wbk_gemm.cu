@@ -361,10 +361,11 @@ __device__ __forceinline__ void epi_values(const Params& p, const uint32_t* acc,
       const uint4 b = bias_pre != nullptr ? bias_pre[q] : __ldg(bv + q);
       const __half2* h = reinterpret_cast<const __half2*>(&b);
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float2 f = __half22float2(h[t]);
-        v[8 * q + 2 * t] = fmaf(__uint_as_float(acc[8 * q + 2 * t]), descale, f.x);
-        v[8 * q + 2 * t + 1] = fmaf(__uint_as_float(acc[8 * q + 2 * t + 1]), descale, f.y);
+      for (int t = 0; t < 4; ++t) {  // fma(acc, descale, bias), two lanes per instruction
+        const float2 r = f2_fma(make_float2(__uint_as_float(acc[8 * q + 2 * t]), __uint_as_float(acc[8 * q + 2 * t + 1])),
+                                make_float2(descale, descale), __half22float2(h[t]));
+        v[8 * q + 2 * t] = r.x;
+        v[8 * q + 2 * t + 1] = r.y;
       }
     }
   } else {
