@@ -251,16 +251,14 @@ template <int kFmt, bool kFin>
 __device__ __forceinline__ void gelu_quantise_vectors(const uint16_t* table, const uint4* __restrict__ yv,
                                                       uint2* __restrict__ qv, int64_t nvec, int64_t tid,
                                                       int64_t stride, float inv, float mx) {
+  constexpr int kU = 8;  // 16-byte loads in flight per thread
   int64_t i = tid;
-  for (; i + 3 * stride < nvec; i += 4 * stride) {
-    const uint4 v0 = ld_stream16(yv + i);
-    const uint4 v1 = ld_stream16(yv + i + stride);
-    const uint4 v2 = ld_stream16(yv + i + 2 * stride);
-    const uint4 v3 = ld_stream16(yv + i + 3 * stride);
-    qv[i] = gelu_q8x8<kFmt, kFin>(table, v0, inv, mx);
-    qv[i + stride] = gelu_q8x8<kFmt, kFin>(table, v1, inv, mx);
-    qv[i + 2 * stride] = gelu_q8x8<kFmt, kFin>(table, v2, inv, mx);
-    qv[i + 3 * stride] = gelu_q8x8<kFmt, kFin>(table, v3, inv, mx);
+  for (; i + (kU - 1) * stride < nvec; i += kU * stride) {
+    uint4 v[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) v[u] = ld_stream16(yv + i + u * stride);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) qv[i + u * stride] = gelu_q8x8<kFmt, kFin>(table, v[u], inv, mx);
   }
   for (; i < nvec; i += stride) qv[i] = gelu_q8x8<kFmt, kFin>(table, ld_stream16(yv + i), inv, mx);
 }
