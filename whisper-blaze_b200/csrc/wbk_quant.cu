@@ -80,15 +80,22 @@ __device__ __forceinline__ void quantise_vectors_back(const uint4* __restrict__ 
   const int64_t rounds = (nvec + stride - 1) / stride;
   const uint64_t drop = l2_policy_evict_first();  // last use of the input
   int64_t r = rounds - 1;
-  for (; r >= 1; r -= 2) {  // rounds r and r - 1 (r - 1 < rounds - 1 is a full round)
-    const int64_t i0 = r * stride + tid, i1 = i0 - stride;
+  constexpr int kU = 4;  // rounds per step: 16-byte loads in flight per thread
+  for (; r >= kU - 1; r -= kU) {  // rounds r .. r - kU + 1 (all but round r are full)
+    uint4 v[kU];
+    const int64_t i0 = r * stride + tid;
     const bool has0 = i0 < nvec;
-    const uint4 v0 = has0 ? ld_stream16_hint(xv + i0, drop) : make_uint4(0u, 0u, 0u, 0u);
-    const uint4 v1 = ld_stream16_hint(xv + i1, drop);
-    if (has0) qv[i0] = q8x8<kFmt, kFin>(v0, inv, max_fp8);
-    qv[i1] = q8x8<kFmt, kFin>(v1, inv, max_fp8);
+    v[0] = has0 ? ld_stream16_hint(xv + i0, drop) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int u = 1; u < kU; ++u) v[u] = ld_stream16_hint(xv + i0 - u * stride, drop);
+    if (has0) qv[i0] = q8x8<kFmt, kFin>(v[0], inv, max_fp8);
+#pragma unroll
+    for (int u = 1; u < kU; ++u) qv[i0 - u * stride] = q8x8<kFmt, kFin>(v[u], inv, max_fp8);
   }
-  if (r == 0 && tid < nvec) qv[tid] = q8x8<kFmt, kFin>(ld_stream16_hint(xv + tid, drop), inv, max_fp8);
+  for (; r >= 0; --r) {  // the last rounds one at a time (round r may be partial only when it is the first)
+    const int64_t i = r * stride + tid;
+    if (i < nvec) qv[i] = q8x8<kFmt, kFin>(ld_stream16_hint(xv + i, drop), inv, max_fp8);
+  }
 }
 
 template <int kFmt, bool kVec>
