@@ -41,13 +41,14 @@ amax_f16_kernel(const __half* __restrict__ x, int64_t n, uint32_t* __restrict__ 
   if (kVec) {
     const int64_t nvec = n >> 3;
     const uint4* xv = reinterpret_cast<const uint4*>(x);
+    constexpr int kU = 8;  // 16-byte loads in flight per thread
     int64_t i = tid;
-    for (; i + 3 * stride < nvec; i += 4 * stride) {
-      const uint4 v0 = ld_stream16_hint(xv + i, keep);
-      const uint4 v1 = ld_stream16_hint(xv + i + stride, keep);
-      const uint4 v2 = ld_stream16_hint(xv + i + 2 * stride, keep);
-      const uint4 v3 = ld_stream16_hint(xv + i + 3 * stride, keep);
-      m = absmax8_acc(absmax8_acc(absmax8_acc(absmax8_acc(m, v0), v1), v2), v3);
+    for (; i + (kU - 1) * stride < nvec; i += kU * stride) {
+      uint4 v[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) v[u] = ld_stream16_hint(xv + i + u * stride, keep);
+#pragma unroll
+      for (int u = 0; u < kU; ++u) m = absmax8_acc(m, v[u]);
     }
     for (; i < nvec; i += stride) m = absmax8_acc(m, ld_stream16_hint(xv + i, keep));
     done = nvec << 3;
