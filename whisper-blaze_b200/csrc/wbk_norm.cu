@@ -159,7 +159,8 @@ enum NormMode { kModeNormal = 0, kModeStats = 1, kModeQuant = 2 };
 // kVpl = 16-byte vectors (8 halves) per lane; the row has D/8 vectors.
 //   kModeNormal: out (+ sum_out, + out_amax) as wbk_layernorm_f16 / wbk_rmsnorm_f16;
 //   kModeStats:  stats[row] = (mean, rstd) and out_amax of the fp16 outputs, nothing else stored;
-//   kModeQuant:  fp8 codes of the fp16 outputs, from stats[] and scale_inv = (scale, 1/scale).
+//   kModeQuant:  fp8 codes of the fp16 outputs, from stats[] and the scale of the statistics pass's
+//                amax (*out_amax), which CTA 0 also stores to scale_inv = (scale, 1/scale) and scale_out.
 // Rows up to 1536 wide (kVpl <= 6) run two CTAs per SM; without a residual
 // operand they are also software-pipelined (two rows in flight per warp).
 template <int kVpl, bool kRms, int kMode, int kFmt>
@@ -167,7 +168,7 @@ __global__ void __launch_bounds__(kThreads, kVpl <= 6 ? 2 : 1)
 norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, const __half* __restrict__ gamma,
                  const __half* __restrict__ beta, __half* __restrict__ out, __half* __restrict__ sum_out,
                  int64_t rows, int D, float eps, uint32_t* __restrict__ out_amax, float2* __restrict__ stats,
-                 const float* __restrict__ scale_inv, uint8_t* __restrict__ q_out, float* __restrict__ scale_out) {
+                 float* __restrict__ scale_inv, uint8_t* __restrict__ q_out, float* __restrict__ scale_out) {
   griddep_launch_dependents();  // a following GEMM may run its prologue meanwhile
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int nvec = D >> 3;
@@ -195,8 +196,15 @@ norm_warp_kernel(const __half* __restrict__ x, const __half* __restrict__ res, c
   float qinv = 0.0f;
   constexpr float kMx = kFmt == WBK_FMT_E4M3 ? 448.0f : 57344.0f;
   if (kMode == kModeQuant) {
-    qinv = scale_inv[1];
-    if (scale_out != nullptr && blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale_inv[0];
+    // The quantiser's scale rule on the amax (the same device function as the scale kernels), so no
+    // separate launch computes it between the two passes.
+    float sc;
+    scale_from_amax(*out_amax, kMx, sc, qinv);
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+      if (scale_out != nullptr) *scale_out = sc;
+      scale_inv[0] = sc;
+      scale_inv[1] = qinv;
+    }
   }
   // Rows are software-pipelined: the loads of this warp's next row are issued
   // before the current row's reductions, so each warp keeps a row in flight.
@@ -473,7 +481,7 @@ int launch_norm(const void* x, const void* res, const void* gamma, const void* b
 // the stats pass and the quantise pass run the same per-row arithmetic).
 template <int kMode, int kFmt>
 int launch_ln_mode(const __half* x, const __half* gamma, const __half* beta, int64_t rows, int D, float eps,
-                   uint32_t* amax, float2* stats, const float* scale_inv, uint8_t* q, float* scale_out, cudaStream_t s) {
+                   uint32_t* amax, float2* stats, float* scale_inv, uint8_t* q, float* scale_out, cudaStream_t s) {
   const int nvec = D / 8;
 #define WBK_LNQ_CASE(V)                                                                                  \
   if (nvec <= 32 * (V)) {                                                                                \
@@ -563,12 +571,13 @@ int wbk_layernorm_quantise_f16(const void* x, const void* gamma, const void* bet
                                                           nullptr, s))
       return e;
   }
-  if (int e = wbk_scale_from_amax(amax_ws, fmt, scale_inv, stream)) return e;
-  if (rows == 0) return WBK_OK;  // scale only (1.0); scale_out is left unwritten like an empty quantise
+  // scale only (1.0); scale_out is left unwritten like an empty quantise
+  if (rows == 0) return wbk_scale_from_amax(amax_ws, fmt, scale_inv, stream);
+  // The quantise pass derives the scale from the amax itself.
   return fmt == WBK_FMT_E4M3
-             ? launch_ln_mode<kModeQuant, WBK_FMT_E4M3>(xh, gh, bh, rows, d, eps, nullptr, stats, scale_inv, q,
+             ? launch_ln_mode<kModeQuant, WBK_FMT_E4M3>(xh, gh, bh, rows, d, eps, amax_ws, stats, scale_inv, q,
                                                          scale_out, s)
-             : launch_ln_mode<kModeQuant, WBK_FMT_E5M2>(xh, gh, bh, rows, d, eps, nullptr, stats, scale_inv, q,
+             : launch_ln_mode<kModeQuant, WBK_FMT_E5M2>(xh, gh, bh, rows, d, eps, amax_ws, stats, scale_inv, q,
                                                          scale_out, s);
 }
 
