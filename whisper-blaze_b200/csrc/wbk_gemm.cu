@@ -2419,6 +2419,12 @@ int wbk_quantise_f16_resident(const void* x, int64_t n, int fmt, void* q_out, fl
                                              amax_ws, sync_ws, timeout)
                         : cudaLaunchKernelEx(&cfg, quantise_resident_kernel<WBK_FMT_E5M2>, xv, nvec, mx, qv, scale_out,
                                              amax_ws, sync_ws, timeout);
+  if (err == cudaErrorCooperativeLaunchTooLarge) {
+    // Not every SM can hold one of its CTAs right now (the device is shared, or partitioned): the
+    // two-kernel path gives the same codes, scale and amax.
+    (void)cudaGetLastError();
+    return wbk_quantise_f16(x, n, fmt, q_out, scale_out, amax_ws, stream);
+  }
   return cuda_check(err, "wbk_quantise_f16_resident launch");
 }
 
