@@ -138,7 +138,7 @@ int wbk_quantise_f16_noalloc(const void* x, int64_t n, int fmt, void* q_out,
  * before first use; every call that completes leaves it zeroed; not used by two
  * calls at once. After a WBK_ERR_DEVICE_TIMEOUT it must be zero-filled again.
  * amax_ws ends holding the amax bits, as in wbk_quantise_f16.
- * When n < 2^22 or n > 100 x 2^20, n % 8 != 0, x is not 16-byte aligned,
+ * When n < 2^22 or n > 88 x 2^20, n % 8 != 0, x is not 16-byte aligned,
  * q_out not 8-byte aligned, sync_ws is NULL, or the device cannot hold one
  * CTA per SM at once (it is shared or partitioned), this is wbk_quantise_f16
  * (same results).

@@ -1424,9 +1424,9 @@ constexpr int kResUnroll = 4;     // 16-byte loads in flight per thread per step
 constexpr size_t kResSmemBytes = static_cast<size_t>(kResSmemVecs) * kResThreads * 16;  // 224 KB
 constexpr int64_t kResMinElems = int64_t{1} << 22;  // below this the plain two-pass quantiser is as fast
 // Above this most of each slice's front misses L2 in phase 2 and the grid-wide
-// arrival costs more than it saves (measured: 100M elements 4 % faster than the
-// two kernels, 123M 2 % slower).
-constexpr int64_t kResMaxElems = int64_t{100} << 20;
+// arrival costs more than it saves (measured against the two-kernel pair on one
+// box: 83.9M elements 69.8 against 73.7 us, 104.9M 92.8 against 89.3 us).
+constexpr int64_t kResMaxElems = int64_t{88} << 20;
 // Front vectors per CTA read with the evict_last hint: the last ~80 MB of the
 // fronts (what L2 can keep for phase 2); earlier ones are read evict_first.
 constexpr int64_t kResKeepVecs = 33792;

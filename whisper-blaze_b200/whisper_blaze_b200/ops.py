@@ -110,7 +110,7 @@ def quantise_from_amax(x: torch.Tensor, amax_ws: torch.Tensor, fmt="e4m3", q_out
 # 16-byte aligned) are quantised by the one-launch resident kernel
 # (wbk_quantise_f16_resident); the library applies the same bounds.
 RESIDENT_QUANT_MIN = 1 << 22
-RESIDENT_QUANT_MAX = 100 << 20
+RESIDENT_QUANT_MAX = 88 << 20
 _RESIDENT_SYNC_OFFSET = 32  # bytes: words 8..11 of the device's shared workspace (the GEMM's use 0..3)
 
 
